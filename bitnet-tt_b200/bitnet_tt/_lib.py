@@ -1,0 +1,277 @@
+"""ctypes binding of the C ABI in include/bitnet_b200.h (libbitnet_b200.so).
+
+Only plain pointers, ints and floats cross the boundary.  Every call raises
+RuntimeError with the library's status string when it returns a non-zero
+status, mirroring the RuntimeError the reference's ttnn ops raise.  The product
+path has no fallback: if the library cannot be loaded, the first call raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+import torch
+
+_PKG_DIR = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_PKG_DIR, "libbitnet_b200.so")
+
+BITNET_OK = 0
+EPI_NONE, EPI_RELU2_MUL, EPI_RESIDUAL_ADD = 0, 1, 2
+PATH_AUTO, PATH_SIMT, PATH_TCGEN05 = 0, 1, 2
+MAX_SEGMENTS = 4
+
+_c_void_p = ctypes.c_void_p
+_c_int = ctypes.c_int
+_c_float = ctypes.c_float
+_c_size_t = ctypes.c_size_t
+
+
+class Segments(ctypes.Structure):
+    """bitnet_segments_t: per-tensor scales of a fused projection."""
+
+    _fields_ = [
+        ("count", ctypes.c_int32),
+        ("end", ctypes.c_int32 * MAX_SEGMENTS),
+        ("scale", ctypes.c_float * MAX_SEGMENTS),
+    ]
+
+    @classmethod
+    def make(cls, ends: list[int], scales: list[float]) -> "Segments":
+        if not 1 <= len(scales) <= MAX_SEGMENTS or len(ends) != len(scales):
+            raise ValueError("segments: 1..4 (end, scale) pairs expected")
+        s = cls()
+        s.count = len(scales)
+        for i, (e, sc) in enumerate(zip(ends, scales)):
+            s.end[i] = int(e)
+            s.scale[i] = float(sc)
+        return s
+
+
+# name -> (restype, argtypes)
+_SIGNATURES = {
+    "bitnet_abi_version": (_c_int, []),
+    "bitnet_status_string": (ctypes.c_char_p, [_c_int]),
+    "bitnet_last_device_status": (_c_int, [ctypes.POINTER(_c_int)]),
+    "bitnet_last_cuda_error": (ctypes.c_char_p, []),
+    "bitnet_set_pdl": (_c_int, [_c_int]),
+    "bitnet_set_tc_split": (_c_int, [_c_int]),
+    "bitnet_set_simt_max_m": (_c_int, [_c_int]),
+    "bitnet_packed_weight_bytes": (_c_size_t, [_c_int, _c_int]),
+    "bitnet_act_bytes": (_c_size_t, [_c_int, _c_int]),
+    "bitnet_act_rows": (_c_int, [_c_int]),
+    "bitnet_pack_ternary": (_c_int, [_c_void_p, _c_int, _c_int, _c_void_p, _c_void_p]),
+    "bitnet_pack_from_canonical": (_c_int, [_c_void_p, _c_int, _c_int, _c_void_p, _c_void_p]),
+    "bitnet_act_quant": (
+        _c_int,
+        [_c_void_p, _c_int, _c_int, _c_int, _c_void_p, _c_float, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
+         _c_void_p],
+    ),
+    "bitnet_bitlinear_q": (
+        _c_int,
+        [_c_void_p, _c_void_p, _c_void_p, _c_int, _c_int, _c_void_p, _c_int, ctypes.POINTER(Segments), _c_int,
+         _c_void_p, _c_void_p, _c_void_p, _c_int, _c_void_p],
+    ),
+    "bitnet_bitlinear": (
+        _c_int,
+        [_c_void_p, _c_int, _c_int, _c_void_p, _c_float, _c_void_p, _c_int, ctypes.POINTER(Segments), _c_int,
+         _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_int, _c_void_p],
+    ),
+    "bitnet_gqa_decode_attention": (
+        _c_int,
+        [_c_void_p, _c_int, _c_int, _c_int, _c_int, _c_void_p, _c_void_p, _c_void_p, _c_int, _c_void_p, _c_void_p,
+         _c_int, _c_float, _c_void_p, _c_void_p],
+    ),
+    "bitnet_lm_head_bytes": (_c_size_t, [_c_int, _c_int]),
+    "bitnet_pack_lm_head": (_c_int, [_c_void_p, _c_int, _c_int, _c_void_p, _c_void_p]),
+    "bitnet_embed_gather": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_int, _c_int, _c_void_p, _c_void_p]),
+    "bitnet_argmax_workspace_bytes": (_c_size_t, [_c_int, _c_int]),
+    "bitnet_lm_head_argmax": (
+        _c_int,
+        [_c_void_p, _c_int, _c_int, _c_void_p, _c_int, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p],
+    ),
+}
+
+_lib = None
+_lock = threading.Lock()
+
+
+def load(path: str | None = None) -> ctypes.CDLL:
+    """Load the library (once) and declare every exported signature."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            p = path or LIB_PATH
+            if not os.path.exists(p):
+                raise RuntimeError(
+                    f"{p} is missing: build it with `python -c 'import __graft_entry__ as g; g.build()'` "
+                    "(the B200 path has no CPU fallback)"
+                )
+            lib = ctypes.CDLL(p)
+            for name, (res, args) in _SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = lib
+    return _lib
+
+
+def exported_symbols() -> list[str]:
+    return list(_SIGNATURES)
+
+
+def status_string(status: int) -> str:
+    return load().bitnet_status_string(int(status)).decode()
+
+
+def check(status: int, what: str) -> None:
+    if status != BITNET_OK:
+        detail = ""
+        if status == -4:
+            detail = f" [{load().bitnet_last_cuda_error().decode()}]"
+        raise RuntimeError(f"{what} failed: {status_string(status)} (status {status}){detail}")
+
+
+def ptr(t: torch.Tensor | None) -> int | None:
+    if t is None:
+        return None
+    if not t.is_cuda:
+        raise RuntimeError("bitnet-tt B200 kernels take CUDA tensors only (no CPU path)")
+    return t.data_ptr()
+
+
+def stream_handle(stream: torch.cuda.Stream | None = None) -> int:
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return s.cuda_stream
+
+
+def last_device_status() -> tuple[int, int]:
+    site = _c_int(0)
+    st = load().bitnet_last_device_status(ctypes.byref(site))
+    return st, site.value
+
+
+# ---------------------------------------------------------------------------
+# thin typed wrappers
+# ---------------------------------------------------------------------------
+def packed_weight_bytes(n: int, k: int) -> int:
+    return int(load().bitnet_packed_weight_bytes(n, k))
+
+
+def act_bytes(m: int, k: int) -> int:
+    return int(load().bitnet_act_bytes(m, k))
+
+
+def act_rows(m: int) -> int:
+    return int(load().bitnet_act_rows(m))
+
+
+def set_pdl(enable: bool) -> None:
+    check(load().bitnet_set_pdl(1 if enable else 0), "bitnet_set_pdl")
+
+
+def set_tc_split(split: int) -> None:
+    check(load().bitnet_set_tc_split(int(split)), "bitnet_set_tc_split")
+
+
+def set_simt_max_m(m: int) -> None:
+    check(load().bitnet_set_simt_max_m(int(m)), "bitnet_set_simt_max_m")
+
+
+def pack_ternary(w_q: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """int8 ternary [N, K] (CUDA) -> device weight layout (uint8)."""
+    if w_q.dtype != torch.int8 or w_q.dim() != 2:
+        raise ValueError("pack_ternary expects an int8 [N, K] tensor")
+    w_q = w_q.contiguous()
+    n, k = w_q.shape
+    if out is None:
+        out = torch.empty(packed_weight_bytes(n, k), dtype=torch.uint8, device=w_q.device)
+    check(load().bitnet_pack_ternary(ptr(w_q), n, k, ptr(out), stream_handle()), "bitnet_pack_ternary")
+    return out
+
+
+def pack_from_canonical(canonical: torch.Tensor, n: int, k: int) -> torch.Tensor:
+    out = torch.empty(packed_weight_bytes(n, k), dtype=torch.uint8, device=canonical.device)
+    check(load().bitnet_pack_from_canonical(ptr(canonical.contiguous()), n, k, ptr(out), stream_handle()),
+          "bitnet_pack_from_canonical")
+    return out
+
+
+class ActBuffers:
+    """Caller-owned quantised-activation buffers for up to `m` tokens x `k` features."""
+
+    def __init__(self, m: int, k: int, device: torch.device | str):
+        self.m, self.k = m, k
+        self.q = torch.empty(act_bytes(m, k), dtype=torch.int8, device=device)
+        rows = act_rows(m)
+        self.row_scale = torch.empty(rows, dtype=torch.float32, device=device)
+        self.row_sum = torch.empty(rows, dtype=torch.int32, device=device)
+
+
+def act_quant(x: torch.Tensor, gamma: torch.Tensor | None, eps: float, bufs: ActBuffers,
+              normed_out: torch.Tensor | None = None) -> None:
+    m, k = x.shape
+    if x.dtype != torch.bfloat16:
+        raise ValueError("activations must be bf16")
+    check(load().bitnet_act_quant(ptr(x), m, k, x.stride(0), ptr(gamma), float(eps), ptr(bufs.q),
+                                  ptr(bufs.row_scale), ptr(bufs.row_sum), ptr(normed_out), stream_handle()),
+          "bitnet_act_quant")
+
+
+def rmsnorm(x: torch.Tensor, gamma: torch.Tensor, eps: float, out: torch.Tensor | None = None) -> torch.Tensor:
+    m, k = x.shape
+    if out is None:
+        out = torch.empty((m, k), dtype=torch.bfloat16, device=x.device)
+    check(load().bitnet_act_quant(ptr(x), m, k, x.stride(0), ptr(gamma), float(eps), None, None, None, ptr(out),
+                                  stream_handle()), "bitnet_act_quant(rmsnorm)")
+    return out
+
+
+def bitlinear_q(bufs: ActBuffers, m: int, k: int, w_packed: torch.Tensor, n: int, segments: Segments | None,
+                epilogue: int, residual: torch.Tensor | None, y: torch.Tensor, acc_out: torch.Tensor | None = None,
+                path: int = PATH_AUTO) -> None:
+    seg = ctypes.byref(segments) if segments is not None else None
+    check(load().bitnet_bitlinear_q(ptr(bufs.q), ptr(bufs.row_scale), ptr(bufs.row_sum), m, k, ptr(w_packed), n,
+                                    seg, epilogue, ptr(residual), ptr(y), ptr(acc_out), path, stream_handle()),
+          "bitnet_bitlinear_q")
+
+
+def gqa_decode_attention(qkv: torch.Tensor, n_heads: int, n_kv: int, head_dim: int, positions: torch.Tensor,
+                         rope_cos: torch.Tensor, rope_sin: torch.Tensor, k_cache: torch.Tensor,
+                         v_cache: torch.Tensor, scale: float, out: torch.Tensor) -> None:
+    b = qkv.shape[0]
+    check(load().bitnet_gqa_decode_attention(ptr(qkv), b, n_heads, n_kv, head_dim, ptr(positions), ptr(rope_cos),
+                                             ptr(rope_sin), rope_cos.shape[0], ptr(k_cache), ptr(v_cache),
+                                             k_cache.shape[2], float(scale), ptr(out), stream_handle()),
+          "bitnet_gqa_decode_attention")
+
+
+def lm_head_bytes(v: int, k: int) -> int:
+    return int(load().bitnet_lm_head_bytes(v, k))
+
+
+def pack_lm_head(w: torch.Tensor) -> torch.Tensor:
+    v, k = w.shape
+    out = torch.empty(lm_head_bytes(v, k), dtype=torch.uint8, device=w.device)
+    check(load().bitnet_pack_lm_head(ptr(w.contiguous()), v, k, ptr(out), stream_handle()), "bitnet_pack_lm_head")
+    return out
+
+
+def embed_gather(ids: torch.Tensor, w_tiled: torch.Tensor, v: int, k: int, out: torch.Tensor) -> None:
+    check(load().bitnet_embed_gather(ptr(ids), ids.numel(), ptr(w_tiled), v, k, ptr(out), stream_handle()),
+          "bitnet_embed_gather")
+
+
+def argmax_workspace_bytes(b: int, v: int) -> int:
+    return int(load().bitnet_argmax_workspace_bytes(b, v))
+
+
+def lm_head_argmax(h: torch.Tensor, w_tiled: torch.Tensor, v: int, workspace: torch.Tensor, out_ids: torch.Tensor,
+                   logits_out: torch.Tensor | None = None, advance_positions: torch.Tensor | None = None) -> None:
+    b, k = h.shape
+    check(load().bitnet_lm_head_argmax(ptr(h), b, k, ptr(w_tiled), v, ptr(workspace), ptr(out_ids),
+                                       ptr(logits_out), ptr(advance_positions), stream_handle()),
+          "bitnet_lm_head_argmax")

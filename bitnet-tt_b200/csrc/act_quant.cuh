@@ -1,0 +1,113 @@
+// Fused RMSNorm + per-token int8 absmax activation quantisation.
+//
+// Semantics (one token row x of K bf16 values, gamma bf16 or absent):
+//   ss     = sum_k x_k^2                         accumulated in fp64
+//   var    = fp32(ss / K)
+//   r      = 1 / sqrt(var + eps)                 fp32, IEEE sqrt and divide
+//   y_k    = bf16(x_k * r)                       HF BitNetRMSNorm: fp32 math, cast to bf16,
+//   a_k    = bf16(gamma_k * y_k)                 then weight * hidden in bf16
+//   amax   = max(max_k |a_k|, 1e-5)
+//   s      = 127 / amax                          (row_scale)
+//   q_k    = clamp(rint(a_k * s), -128, 127)     half-to-even, as np.round / torch.round
+//   sum    = sum_k q_k                           (row_sum, used by the ternary epilogue)
+// Without gamma, a_k = x_k.  Every fp32 operation is an explicit _rn intrinsic so
+// the compiler cannot contract or reorder it; the fp64 sum of squares of bf16
+// values is exact for any summation order whenever the squares span less than
+// 2^37 in magnitude, so the codes do not depend on the reduction tree.
+#pragma once
+#include "common.cuh"
+
+namespace bitnet {
+
+template <typename T, typename Op>
+__device__ __forceinline__ T block_reduce(T v, T* scratch, Op op) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = op(v, __shfl_xor_sync(0xffffffffu, v, o));
+  __syncthreads();  // protect scratch from a previous use
+  if (lane == 0) scratch[warp] = v;
+  __syncthreads();
+  const int nw = blockDim.x >> 5;
+  T r = scratch[0];
+  for (int i = 1; i < nw; ++i) r = op(r, scratch[i]);
+  return r;
+}
+
+struct OpAddD { __device__ double operator()(double a, double b) const { return a + b; } };
+struct OpMaxF { __device__ float operator()(float a, float b) const { return fmaxf(a, b); } };
+struct OpAddI { __device__ int operator()(int a, int b) const { return a + b; } };
+
+// grid = act_rows(M) (one CTA per padded token row), block = 256,
+// dynamic smem = Kp * 4 bytes.
+__global__ void __launch_bounds__(256)
+act_quant_kernel(const uint16_t* __restrict__ x, int M, int K, int ldx, const uint16_t* __restrict__ gamma,
+                 float eps, int8_t* __restrict__ q, float* __restrict__ row_scale, int32_t* __restrict__ row_sum,
+                 uint16_t* __restrict__ normed_out, int T, int Kp) {
+  extern __shared__ float sval[];
+  __shared__ double red_d[32];
+  __shared__ float red_f[32];
+  __shared__ int red_i[32];
+
+  pdl_wait();
+  const int m = blockIdx.x;
+  const int tid = threadIdx.x, nt = blockDim.x;
+  const bool valid = m < M;
+
+  double ss = 0.0;
+  for (int k = tid; k < Kp; k += nt) {
+    float v = 0.f;
+    if (valid && k < K) v = bf16_bits_to_f32(x[(size_t)m * ldx + k]);
+    sval[k] = v;
+    ss += (double)v * (double)v;
+  }
+
+  if (gamma != nullptr) {
+    ss = block_reduce(ss, red_d, OpAddD());
+    const float var = __double2float_rn(__ddiv_rn(ss, (double)K));
+    const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+    for (int k = tid; k < K; k += nt) {
+      const float y = round_bf16(__fmul_rn(sval[k], r));
+      sval[k] = round_bf16(__fmul_rn(bf16_bits_to_f32(gamma[k]), y));
+    }
+  }
+  __syncthreads();
+
+  if (normed_out != nullptr && valid) {
+    for (int k = tid; k < K; k += nt) normed_out[(size_t)m * K + k] = f32_to_bf16_bits(sval[k]);
+  }
+  if (q == nullptr) {
+    pdl_trigger();
+    return;
+  }
+
+  float amax = 0.f;
+  for (int k = tid; k < K; k += nt) amax = fmaxf(amax, fabsf(sval[k]));
+  amax = block_reduce(amax, red_f, OpMaxF());
+  amax = fmaxf(amax, 1e-5f);
+  const float s = __fdiv_rn(127.0f, amax);
+
+  int qsum = 0;
+  for (int k4 = tid * 4; k4 < Kp; k4 += nt * 4) {
+    uint32_t word = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int k = k4 + i;
+      int qi = 0;
+      if (valid && k < K) {
+        qi = __float2int_rn(__fmul_rn(sval[k], s));
+        qi = max(-128, min(127, qi));
+      }
+      qsum += qi;
+      word |= ((uint32_t)(qi & 0xFF)) << (8 * i);
+    }
+    *reinterpret_cast<uint32_t*>(q + alayout_offset(m, k4, T, Kp)) = word;
+  }
+  qsum = block_reduce(qsum, red_i, OpAddI());
+  if (tid == 0) {
+    row_scale[m] = valid ? s : 1.0f;
+    row_sum[m] = qsum;
+  }
+  pdl_trigger();
+}
+
+}  // namespace bitnet

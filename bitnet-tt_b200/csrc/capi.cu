@@ -1,0 +1,481 @@
+// C ABI of the B200 packed-ternary BitLinear decode path (declared in
+// include/bitnet_b200.h).  One translation unit: every kernel header is
+// included here so the kernels share the device status word.
+//
+// Host-side responsibilities: argument validation (shapes, alignment, device
+// architecture), choice of execution path and K split, and kernel launches
+// with programmatic-dependent-launch and cluster attributes.  No entry point
+// allocates device memory or synchronises (except bitnet_last_device_status).
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "act_quant.cuh"
+#include "attention.cuh"
+#include "bitlinear_simt.cuh"
+#include "bitlinear_tc.cuh"
+#include "common.cuh"
+#include "lm_head.cuh"
+#include "pack.cuh"
+#include "../../include/bitnet_b200.h"
+
+using namespace bitnet;
+
+namespace {
+
+constexpr int kAbiVersion = 1;
+constexpr int kMaxDevices = 64;
+constexpr size_t kMaxDynSmem = 232448;  // 227 KB, the sm_100 per-CTA opt-in limit
+
+std::atomic<int> g_pdl{1};        // programmatic dependent launch on by default
+std::atomic<int> g_tc_split{0};   // 0 = automatic K split for the tcgen05 path
+std::atomic<int> g_simt_max_m{4}; // AUTO path: SIMT for M <= this
+
+struct DevInfo {
+  int checked = 0;  // 0 unknown, 1 ok, -1 unsupported
+  int sms = 0;
+};
+DevInfo g_dev[kMaxDevices];
+std::mutex g_mu;
+
+int device_info(DevInfo** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return BITNET_ERR_CUDA;
+  DevInfo& d = g_dev[dev];
+  if (d.checked == 0) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (d.checked == 0) {
+      int major = 0, minor = 0, sms = 0;
+      if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+          cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess ||
+          cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+        return BITNET_ERR_CUDA;
+      d.sms = sms;
+      d.checked = (major == 10 && minor == 0) ? 1 : -1;
+    }
+  }
+  if (d.checked < 0) return BITNET_ERR_UNSUPPORTED_DEVICE;
+  *out = &d;
+  return BITNET_OK;
+}
+
+thread_local char g_cuda_msg[256] = "no CUDA error recorded";
+
+int cuda_fail(cudaError_t e, const char* what) {
+  snprintf(g_cuda_msg, sizeof(g_cuda_msg), "%s: %s (%d)", what, cudaGetErrorString(e), (int)e);
+  (void)cudaGetLastError();
+  return BITNET_ERR_CUDA;
+}
+
+// Raise the dynamic shared memory limit of a kernel once per device, to the
+// per-CTA opt-in limit minus the kernel's static shared memory.
+template <typename K>
+int ensure_smem(K kernel, std::atomic<unsigned long long>* done_mask) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (done_mask->load() & bit) return BITNET_OK;
+  cudaFuncAttributes fa;
+  cudaError_t e = cudaFuncGetAttributes(&fa, kernel);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncGetAttributes");
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)(kMaxDynSmem - fa.sharedSizeBytes));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
+  done_mask->fetch_or(bit);
+  return BITNET_OK;
+}
+
+template <typename... KArgs, typename... Args>
+int launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, bitnet_stream_t stream, int cluster_z,
+           Args... args) {
+  cudaLaunchConfig_t cfg;
+  memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = (cudaStream_t)stream;
+  cudaLaunchAttribute attrs[2];
+  int n = 0;
+  if (g_pdl.load()) {
+    attrs[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (cluster_z > 1) {
+    attrs[n].id = cudaLaunchAttributeClusterDimension;
+    attrs[n].val.clusterDim.x = 1;
+    attrs[n].val.clusterDim.y = 1;
+    attrs[n].val.clusterDim.z = (unsigned)cluster_z;
+    ++n;
+  }
+  cfg.attrs = attrs;
+  cfg.numAttrs = n;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, ((KArgs)args)...);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx");
+  return BITNET_OK;
+}
+
+inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+inline int round_up(int x, int m) { return (x + m - 1) / m * m; }
+
+int act_rows_of(int M) { return M <= 256 ? round_up(M, 16) : round_up(M, 256); }
+int act_tile_of(int M) { return M <= 256 ? round_up(M, 16) : 256; }
+
+int to_dev_segments(const bitnet_segments_t* s, int N, int epilogue, bitnet_segments_dev* out) {
+  memset(out, 0, sizeof(*out));
+  if (s == nullptr) {
+    out->count = 1;
+    out->end[0] = N;
+    out->scale[0] = out->scale[1] = 1.0f;
+    if (epilogue == BITNET_EPI_RELU2_MUL) out->count = 2;
+    return BITNET_OK;
+  }
+  if (s->count < 1 || s->count > BITNET_MAX_SEGMENTS) return BITNET_ERR_INVALID_ARGUMENT;
+  out->count = s->count;
+  for (int i = 0; i < s->count; ++i) {
+    out->end[i] = s->end[i];
+    out->scale[i] = s->scale[i];
+  }
+  if (epilogue == BITNET_EPI_RELU2_MUL) return s->count == 2 ? BITNET_OK : BITNET_ERR_INVALID_ARGUMENT;
+  for (int i = 0; i < s->count; ++i)
+    if (s->end[i] <= (i ? s->end[i - 1] : 0)) return BITNET_ERR_INVALID_ARGUMENT;
+  return s->end[s->count - 1] == N ? BITNET_OK : BITNET_ERR_INVALID_ARGUMENT;
+}
+
+std::atomic<unsigned long long> g_smem_aq{0}, g_smem_simt[3][4], g_smem_tc[3], g_smem_lmh{0};
+
+template <int EPI, int MT>
+int launch_simt(const int8_t* q, const float* rs, const int32_t* rsum, int M, int Kp, int T, const uint8_t* w,
+                int N, const bitnet_segments_dev& seg, const uint16_t* res, uint16_t* y, int32_t* acc,
+                bitnet_stream_t st, int mt_idx) {
+  auto k = bitlinear_simt_kernel<EPI, MT>;
+  if (int e = ensure_smem(k, &g_smem_simt[EPI][mt_idx])) return e;
+  const int rows = 32 * (EPI == EPI_RELU2_MUL ? 2 : 1);
+  const size_t smem = (size_t)Kp * 8 + (size_t)8 * MT * 32 * 4;
+  if (smem > kMaxDynSmem) return BITNET_ERR_INVALID_ARGUMENT;
+  return launch(k, dim3((N + rows - 1) / rows), dim3(SIMT_THREADS), smem, st, 1, q, rs, rsum, M, Kp, T, w, N, seg,
+                res, y, acc);
+}
+
+template <int EPI>
+int dispatch_simt(const int8_t* q, const float* rs, const int32_t* rsum, int M, int Kp, int T, const uint8_t* w,
+                  int N, const bitnet_segments_dev& seg, const uint16_t* res, uint16_t* y, int32_t* acc,
+                  bitnet_stream_t st) {
+  if (M <= 1) return launch_simt<EPI, 1>(q, rs, rsum, M, Kp, T, w, N, seg, res, y, acc, st, 0);
+  if (M <= 2) return launch_simt<EPI, 2>(q, rs, rsum, M, Kp, T, w, N, seg, res, y, acc, st, 1);
+  if (M <= 4) return launch_simt<EPI, 4>(q, rs, rsum, M, Kp, T, w, N, seg, res, y, acc, st, 2);
+  return launch_simt<EPI, 8>(q, rs, rsum, M, Kp, T, w, N, seg, res, y, acc, st, 3);
+}
+
+// Shared-memory request of the tcgen05 BitLinear.  Besides the ring and the
+// epilogue buffers it has a floor that caps the number of resident CTAs per SM
+// to what tensor memory can serve at once (two 256-column CTAs, or one
+// 512-column CTA): every resident CTA then gets its columns immediately, so a
+// CTA of a cluster can never sit in tcgen05.alloc while its peers wait for it
+// at the cluster barrier.
+size_t tc_smem_bytes(int T, int nslot, int split) {
+  const size_t ring = (size_t)nslot * tc_slot_bytes(T);
+  const size_t stage = (size_t)128 * (T + 1) * 4;
+  const int tok_cap = (T + split - 1) / split;
+  const size_t recv = (size_t)split * 128 * (tok_cap + 1) * 4;
+  size_t bytes = TC_CTRL_BYTES + (split > 1 ? ring + recv : (ring > stage ? ring : stage));
+  const size_t floor_bytes = tc_tmem_cols(T) == 512 ? (size_t)116 * 1024 : (size_t)80 * 1024;
+  return bytes < floor_bytes ? floor_bytes : bytes;
+}
+
+template <int EPI>
+int dispatch_tc(TcParams p, int ntile_n, int ntile_m, bitnet_stream_t st, const DevInfo& dev) {
+  auto k = bitlinear_tc_kernel<EPI>;
+  if (int e = ensure_smem(k, &g_smem_tc[EPI])) return e;
+  const int tiles = ntile_n * ntile_m;
+  int split = g_tc_split.load();
+  if (split <= 0) {
+    split = 1;
+    if (ntile_m == 1 && p.T <= 64) {
+      split = dev.sms / tiles;
+      if (split > 8) split = 8;
+      const int by_k = p.KC / 4;  // at least one full 256-wide stage per CTA
+      if (split > by_k) split = by_k;
+      if (split < 1) split = 1;
+    }
+  }
+  if (split > 8 || split > p.KC) return BITNET_ERR_INVALID_ARGUMENT;
+  if (split > 1 && p.T > 64) return BITNET_ERR_INVALID_ARGUMENT;
+  const int chunks_max = (p.KC + split - 1) / split;
+  const int stages_max = (chunks_max + TC_STAGE_CHUNKS - 1) / TC_STAGE_CHUNKS;
+  int nslot = TC_MAX_SLOTS;
+  if (nslot > stages_max) nslot = stages_max;
+  if (nslot < 2) nslot = 2;
+  while (nslot > 2 && tc_smem_bytes(p.T, nslot, split) > kMaxDynSmem) --nslot;
+  const size_t smem = tc_smem_bytes(p.T, nslot, split);
+  if (smem > kMaxDynSmem) return BITNET_ERR_INVALID_ARGUMENT;
+  p.nslot = nslot;
+  p.split = split;
+  return launch(k, dim3(ntile_n, ntile_m, split), dim3(TC_THREADS), smem, st, split, p);
+}
+
+}  // namespace
+
+extern "C" {
+
+int bitnet_abi_version(void) { return kAbiVersion; }
+
+const char* bitnet_last_cuda_error(void) { return g_cuda_msg; }
+
+const char* bitnet_status_string(int status) {
+  switch (status) {
+    case BITNET_OK: return "ok";
+    case BITNET_ERR_INVALID_ARGUMENT: return "invalid argument (shape, null pointer or option out of range)";
+    case BITNET_ERR_ALIGNMENT: return "pointer not aligned as required";
+    case BITNET_ERR_UNSUPPORTED_DEVICE: return "current CUDA device is not an sm_100 (B200) GPU";
+    case BITNET_ERR_CUDA: return "CUDA runtime call failed";
+    case BITNET_ERR_DEVICE_TIMEOUT: return "a kernel gave up a bounded wait on the device";
+    default: return "unknown status";
+  }
+}
+
+int bitnet_last_device_status(int* site) {
+  if (cudaDeviceSynchronize() != cudaSuccess) return BITNET_ERR_CUDA;
+  int st = 0, where = 0, zero = 0;
+  if (cudaMemcpyFromSymbol(&st, g_bitnet_dev_status, sizeof(int)) != cudaSuccess) return BITNET_ERR_CUDA;
+  if (cudaMemcpyFromSymbol(&where, g_bitnet_dev_site, sizeof(int)) != cudaSuccess) return BITNET_ERR_CUDA;
+  if (st != 0) {
+    cudaMemcpyToSymbol(g_bitnet_dev_status, &zero, sizeof(int));
+    cudaMemcpyToSymbol(g_bitnet_dev_site, &zero, sizeof(int));
+  }
+  if (site) *site = where;
+  if (st == DEV_ERR_TIMEOUT) return BITNET_ERR_DEVICE_TIMEOUT;
+  if (st == DEV_ERR_BOUNDS) return BITNET_ERR_INVALID_ARGUMENT;
+  return BITNET_OK;
+}
+
+int bitnet_set_pdl(int enable) {
+  g_pdl.store(enable ? 1 : 0);
+  return BITNET_OK;
+}
+int bitnet_set_tc_split(int split) {
+  if (split < 0 || split > 8) return BITNET_ERR_INVALID_ARGUMENT;
+  g_tc_split.store(split);
+  return BITNET_OK;
+}
+int bitnet_set_simt_max_m(int m) {
+  if (m < 0 || m > SIMT_MAX_M) return BITNET_ERR_INVALID_ARGUMENT;
+  g_simt_max_m.store(m);
+  return BITNET_OK;
+}
+
+size_t bitnet_packed_weight_bytes(int N, int K) {
+  if (N <= 0 || K <= 0) return 0;
+  return (size_t)round_up(N, 128) * (size_t)(round_up(K, 64) / 4);
+}
+size_t bitnet_act_bytes(int M, int K) {
+  if (M <= 0 || K <= 0) return 0;
+  return (size_t)act_rows_of(M) * (size_t)round_up(K, 64);
+}
+int bitnet_act_rows(int M) { return M <= 0 ? 0 : act_rows_of(M); }
+
+static int grid_for(size_t work, int threads) {
+  size_t g = (work + threads - 1) / threads;
+  if (g > 65535u * 4u) g = 65535u * 4u;
+  return (int)(g == 0 ? 1 : g);
+}
+
+int bitnet_pack_ternary(const int8_t* w_q, int N, int K, uint8_t* w_packed, bitnet_stream_t stream) {
+  DevInfo* d;
+  if (int e = device_info(&d)) return e;
+  if (!w_q || !w_packed || N <= 0 || K <= 0) return BITNET_ERR_INVALID_ARGUMENT;
+  if (!aligned(w_packed, 16)) return BITNET_ERR_ALIGNMENT;
+  const int Npad = round_up(N, 128), KC = round_up(K, 64) / 64;
+  const size_t words = (size_t)Npad * KC * 4;
+  pack_ternary_kernel<<<grid_for(words, 256), 256, 0, (cudaStream_t)stream>>>(w_q, N, K, Npad, KC,
+                                                                              reinterpret_cast<uint32_t*>(w_packed));
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? BITNET_OK : cuda_fail(e, "kernel launch");
+}
+
+int bitnet_pack_from_canonical(const uint8_t* canonical, int N, int K, uint8_t* w_packed, bitnet_stream_t stream) {
+  DevInfo* d;
+  if (int e = device_info(&d)) return e;
+  if (!canonical || !w_packed || N <= 0 || K <= 0) return BITNET_ERR_INVALID_ARGUMENT;
+  if (!aligned(w_packed, 16)) return BITNET_ERR_ALIGNMENT;
+  const int Npad = round_up(N, 128), KC = round_up(K, 64) / 64;
+  const size_t words = (size_t)Npad * KC * 4;
+  pack_from_canonical_kernel<<<grid_for(words, 256), 256, 0, (cudaStream_t)stream>>>(
+      canonical, N, K, Npad, KC, reinterpret_cast<uint32_t*>(w_packed));
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? BITNET_OK : cuda_fail(e, "kernel launch");
+}
+
+int bitnet_act_quant(const void* x, int M, int K, int ldx, const void* gamma, float eps, int8_t* q, float* row_scale,
+                     int32_t* row_sum, void* normed_out, bitnet_stream_t stream) {
+  DevInfo* d;
+  if (int e = device_info(&d)) return e;
+  if (!x || M <= 0 || K <= 0 || ldx < K) return BITNET_ERR_INVALID_ARGUMENT;
+  const bool want_q = q || row_scale || row_sum;
+  if (want_q && (!q || !row_scale || !row_sum)) return BITNET_ERR_INVALID_ARGUMENT;
+  if (!want_q && !normed_out) return BITNET_ERR_INVALID_ARGUMENT;
+  if (!(eps >= 0.f)) return BITNET_ERR_INVALID_ARGUMENT;
+  if (!aligned(x, 2) || (gamma && !aligned(gamma, 2)) || (normed_out && !aligned(normed_out, 2)))
+    return BITNET_ERR_ALIGNMENT;
+  if (q && !aligned(q, 16)) return BITNET_ERR_ALIGNMENT;
+  const int Kp = round_up(K, 64);
+  const size_t smem = (size_t)Kp * 4;
+  if (smem > kMaxDynSmem) return BITNET_ERR_INVALID_ARGUMENT;
+  if (int e = ensure_smem(act_quant_kernel, &g_smem_aq)) return e;
+  const int rows = want_q ? act_rows_of(M) : M;
+  return launch(act_quant_kernel, dim3(rows), dim3(256), smem, stream, 1, (const uint16_t*)x, M, K, ldx,
+                (const uint16_t*)gamma, eps, q, row_scale, row_sum, (uint16_t*)normed_out, act_tile_of(M), Kp);
+}
+
+int bitnet_bitlinear_q(const int8_t* q, const float* row_scale, const int32_t* row_sum, int M, int K,
+                       const uint8_t* w_packed, int N, const bitnet_segments_t* segments, int epilogue,
+                       const void* residual, void* y, int32_t* acc_out, int path, bitnet_stream_t stream) {
+  DevInfo* d;
+  if (int e = device_info(&d)) return e;
+  if (!q || !row_scale || !row_sum || !w_packed || !y || M <= 0 || K <= 0 || N <= 0)
+    return BITNET_ERR_INVALID_ARGUMENT;
+  if (epilogue < BITNET_EPI_NONE || epilogue > BITNET_EPI_RESIDUAL_ADD) return BITNET_ERR_INVALID_ARGUMENT;
+  if (epilogue == BITNET_EPI_RESIDUAL_ADD && !residual) return BITNET_ERR_INVALID_ARGUMENT;
+  if (epilogue == BITNET_EPI_RELU2_MUL && (N % 64) != 0) return BITNET_ERR_INVALID_ARGUMENT;
+  if (!aligned(q, 16) || !aligned(w_packed, 16) || !aligned(row_scale, 4) || !aligned(row_sum, 4) ||
+      !aligned(y, 2) || (residual && !aligned(residual, 2)) || (acc_out && !aligned(acc_out, 4)))
+    return BITNET_ERR_ALIGNMENT;
+  bitnet_segments_dev seg;
+  if (int e = to_dev_segments(segments, N, epilogue, &seg)) return e;
+  const int Kp = round_up(K, 64), T = act_tile_of(M);
+  if (path == BITNET_PATH_AUTO) path = (M <= g_simt_max_m.load()) ? BITNET_PATH_SIMT : BITNET_PATH_TCGEN05;
+  const uint16_t* res = (const uint16_t*)residual;
+  uint16_t* yy = (uint16_t*)y;
+  if (path == BITNET_PATH_SIMT) {
+    if (M > SIMT_MAX_M) return BITNET_ERR_INVALID_ARGUMENT;
+    switch (epilogue) {
+      case BITNET_EPI_NONE: return dispatch_simt<EPI_NONE>(q, row_scale, row_sum, M, Kp, T, w_packed, N, seg, res, yy, acc_out, stream);
+      case BITNET_EPI_RELU2_MUL: return dispatch_simt<EPI_RELU2_MUL>(q, row_scale, row_sum, M, Kp, T, w_packed, N, seg, res, yy, acc_out, stream);
+      default: return dispatch_simt<EPI_RESIDUAL_ADD>(q, row_scale, row_sum, M, Kp, T, w_packed, N, seg, res, yy, acc_out, stream);
+    }
+  }
+  if (path != BITNET_PATH_TCGEN05) return BITNET_ERR_INVALID_ARGUMENT;
+  TcParams p;
+  memset(&p, 0, sizeof(p));
+  p.q = q;
+  p.row_scale = row_scale;
+  p.row_sum = row_sum;
+  p.M = M;
+  p.Kp = Kp;
+  p.T = T;
+  p.w = w_packed;
+  p.N = N;
+  p.KC = Kp / 64;
+  p.seg = seg;
+  p.residual = res;
+  p.y = yy;
+  p.acc_out = acc_out;
+  const int ntile_n = round_up(N, 128) / 128, ntile_m = act_rows_of(M) / T;
+  switch (epilogue) {
+    case BITNET_EPI_NONE: return dispatch_tc<EPI_NONE>(p, ntile_n, ntile_m, stream, *d);
+    case BITNET_EPI_RELU2_MUL: return dispatch_tc<EPI_RELU2_MUL>(p, ntile_n, ntile_m, stream, *d);
+    default: return dispatch_tc<EPI_RESIDUAL_ADD>(p, ntile_n, ntile_m, stream, *d);
+  }
+}
+
+int bitnet_bitlinear(const void* x, int M, int K, const void* gamma, float eps, const uint8_t* w_packed, int N,
+                     const bitnet_segments_t* segments, int epilogue, const void* residual, void* y, int32_t* acc_out,
+                     int8_t* q_ws, float* scale_ws, int32_t* sum_ws, int path, bitnet_stream_t stream) {
+  if (!q_ws || !scale_ws || !sum_ws) return BITNET_ERR_INVALID_ARGUMENT;
+  if (int e = bitnet_act_quant(x, M, K, K, gamma, eps, q_ws, scale_ws, sum_ws, nullptr, stream)) return e;
+  return bitnet_bitlinear_q(q_ws, scale_ws, sum_ws, M, K, w_packed, N, segments, epilogue, residual, y, acc_out,
+                            path, stream);
+}
+
+int bitnet_gqa_decode_attention(const void* qkv, int B, int n_heads, int n_kv_heads, int head_dim,
+                                const int32_t* positions, const void* rope_cos, const void* rope_sin, int rope_len,
+                                void* k_cache, void* v_cache, int max_len, float scale, void* out,
+                                bitnet_stream_t stream) {
+  DevInfo* d;
+  if (int e = device_info(&d)) return e;
+  if (!qkv || !positions || !rope_cos || !rope_sin || !k_cache || !v_cache || !out) return BITNET_ERR_INVALID_ARGUMENT;
+  if (B <= 0 || n_kv_heads <= 0 || n_heads <= 0 || n_heads % n_kv_heads != 0 || head_dim != ATT_D || max_len <= 0 ||
+      rope_len <= 0)
+    return BITNET_ERR_INVALID_ARGUMENT;
+  if (!aligned(k_cache, 16) || !aligned(v_cache, 16) || !aligned(qkv, 2) || !aligned(out, 2))
+    return BITNET_ERR_ALIGNMENT;
+  AttnParams p;
+  p.qkv = (const uint16_t*)qkv;
+  p.n_heads = n_heads;
+  p.n_kv = n_kv_heads;
+  p.G = n_heads / n_kv_heads;
+  p.positions = positions;
+  p.rope_cos = (const uint16_t*)rope_cos;
+  p.rope_sin = (const uint16_t*)rope_sin;
+  p.rope_len = rope_len;
+  p.k_cache = (uint16_t*)k_cache;
+  p.v_cache = (uint16_t*)v_cache;
+  p.max_len = max_len;
+  p.scale = scale;
+  p.out = (uint16_t*)out;
+  const dim3 grid(B, n_kv_heads), block(ATT_THREADS);
+  switch (p.G) {
+    case 1: return launch(gqa_decode_kernel<1>, grid, block, 0, stream, 1, p);
+    case 2: return launch(gqa_decode_kernel<2>, grid, block, 0, stream, 1, p);
+    case 4: return launch(gqa_decode_kernel<4>, grid, block, 0, stream, 1, p);
+    case 8: return launch(gqa_decode_kernel<8>, grid, block, 0, stream, 1, p);
+    default: return BITNET_ERR_INVALID_ARGUMENT;
+  }
+}
+
+size_t bitnet_lm_head_bytes(int V, int K) {
+  if (V <= 0 || K <= 0) return 0;
+  return (size_t)round_up(V, 128) * (size_t)round_up(K, 8) * 2;
+}
+
+int bitnet_pack_lm_head(const void* w, int V, int K, void* w_tiled, bitnet_stream_t stream) {
+  DevInfo* d;
+  if (int e = device_info(&d)) return e;
+  if (!w || !w_tiled || V <= 0 || K <= 0) return BITNET_ERR_INVALID_ARGUMENT;
+  if (!aligned(w_tiled, 16) || !aligned(w, 2)) return BITNET_ERR_ALIGNMENT;
+  const int Vpad = round_up(V, 128), KC8 = round_up(K, 8) / 8;
+  pack_lm_head_kernel<<<grid_for((size_t)Vpad * KC8, 256), 256, 0, (cudaStream_t)stream>>>(
+      (const uint16_t*)w, V, K, Vpad, KC8, (uint4*)w_tiled);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? BITNET_OK : cuda_fail(e, "kernel launch");
+}
+
+int bitnet_embed_gather(const int32_t* ids, int B, const void* w_tiled, int V, int K, void* out,
+                        bitnet_stream_t stream) {
+  DevInfo* d;
+  if (int e = device_info(&d)) return e;
+  if (!ids || !w_tiled || !out || B <= 0 || V <= 0 || K <= 0) return BITNET_ERR_INVALID_ARGUMENT;
+  if (!aligned(w_tiled, 16) || !aligned(out, 2)) return BITNET_ERR_ALIGNMENT;
+  const int KC8 = round_up(K, 8) / 8;
+  return launch(embed_gather_kernel, dim3((KC8 + 127) / 128, B), dim3(128), 0, stream, 1, ids, B,
+                (const uint4*)w_tiled, V, K, KC8, (uint16_t*)out);
+}
+
+size_t bitnet_argmax_workspace_bytes(int B, int V) {
+  if (B <= 0 || V <= 0) return 0;
+  return (size_t)(round_up(V, 128) / 128) * (size_t)B * sizeof(ArgPair);
+}
+
+int bitnet_lm_head_argmax(const void* h, int B, int K, const void* w_tiled, int V, void* workspace, int32_t* out_ids,
+                          void* logits_out, int32_t* advance_positions, bitnet_stream_t stream) {
+  DevInfo* d;
+  if (int e = device_info(&d)) return e;
+  if (!h || !w_tiled || !workspace || !out_ids || B <= 0 || B > LMH_TOK || V <= 0 || K <= 0)
+    return BITNET_ERR_INVALID_ARGUMENT;
+  if (!aligned(w_tiled, 16) || !aligned(workspace, 8) || !aligned(h, 2)) return BITNET_ERR_ALIGNMENT;
+  const int KC8 = round_up(K, 8) / 8, ntiles = round_up(V, 128) / 128;
+  const size_t smem = (size_t)KC8 * B * 16;
+  if (smem > kMaxDynSmem) return BITNET_ERR_INVALID_ARGUMENT;
+  if (int e = ensure_smem(lm_head_simt_kernel, &g_smem_lmh)) return e;
+  ArgPair* part = (ArgPair*)workspace;
+  if (int e = launch(lm_head_simt_kernel, dim3(ntiles), dim3(LMH_THREADS), smem, stream, 1, (const uint16_t*)h, B, K,
+                     (const uint4*)w_tiled, V, KC8, part, (uint16_t*)logits_out))
+    return e;
+  return launch(argmax_reduce_kernel, dim3(B), dim3(256), 0, stream, 1, (const ArgPair*)part, ntiles, B, out_ids,
+                advance_positions);
+}
+
+}  // extern "C"

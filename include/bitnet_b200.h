@@ -1,0 +1,177 @@
+/*
+ * bitnet_b200.h -- C ABI of the B200 (sm_100a) packed-ternary BitLinear decode path.
+ *
+ * All tensor pointers are DEVICE pointers owned by the caller.  No entry point
+ * allocates memory, synchronises the device or writes host memory; every launch
+ * is ordered on the stream passed in (a cudaStream_t; NULL is the legacy default
+ * stream), so all of them can be recorded into a CUDA graph.  Every entry point
+ * returns 0 (BITNET_OK) or a negative status; bitnet_status_string() names it.
+ * Nothing throws across the ABI.  Calls on distinct streams with distinct
+ * output buffers are independent.
+ *
+ * bf16 tensors are passed as `void*` and are IEEE bfloat16 (torch.bfloat16).
+ *
+ * The reference project drives this path through ttnn (Tenstorrent) ops; each
+ * declaration below names the reference interface it replaces
+ * (path:line inside deveworld/bitnet-tt).
+ */
+#ifndef BITNET_B200_H
+#define BITNET_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef void* bitnet_stream_t; /* cudaStream_t */
+
+/* ---- status codes ------------------------------------------------------ */
+#define BITNET_OK 0
+#define BITNET_ERR_INVALID_ARGUMENT (-1) /* shape, null pointer or option out of range   */
+#define BITNET_ERR_ALIGNMENT (-2)        /* a pointer is not aligned as documented          */
+#define BITNET_ERR_UNSUPPORTED_DEVICE (-3) /* the current device is not sm_100             */
+#define BITNET_ERR_CUDA (-4)             /* a CUDA runtime call (launch, attribute) failed  */
+#define BITNET_ERR_DEVICE_TIMEOUT (-5)   /* a kernel gave up a bounded wait (see below)     */
+
+/* ---- BitLinear epilogues ------------------------------------------------ */
+#define BITNET_EPI_NONE 0          /* y = bf16(acc * w_scale / s_m)                                */
+#define BITNET_EPI_RELU2_MUL 1     /* rows in 64-row groups [32 gate | 32 up]: y = relu(g)^2 * u   */
+#define BITNET_EPI_RESIDUAL_ADD 2  /* y = bf16(residual + bf16(acc * w_scale / s_m))               */
+
+/* ---- BitLinear execution paths ------------------------------------------ */
+#define BITNET_PATH_AUTO 0    /* SIMT below the ridge batch, tcgen05 above it               */
+#define BITNET_PATH_SIMT 1    /* CUDA-core unpack + dp4a, HBM-bound for M <= 4              */
+#define BITNET_PATH_TCGEN05 2 /* tcgen05 kind::i8 MMA, weights unpacked into TMEM        */
+
+#define BITNET_MAX_SEGMENTS 4
+/* Per-tensor weight scales of a fused projection (QKV has 3 segments, a plain
+ * projection 1).  Segment i covers output rows [end[i-1], end[i]).  For the
+ * RELU2_MUL epilogue scale[0] is the gate scale and scale[1] the up scale. */
+typedef struct {
+  int32_t count;
+  int32_t end[BITNET_MAX_SEGMENTS];
+  float scale[BITNET_MAX_SEGMENTS];
+} bitnet_segments_t;
+
+/* ---- library information -------------------------------------------------- */
+int bitnet_abi_version(void);
+const char* bitnet_status_string(int status);
+/* Reads and clears the library's device status word (set by a kernel that gave
+ * up a bounded wait).  Synchronises the current device.  *site (nullable)
+ * receives the id of the wait that gave up. */
+int bitnet_last_device_status(int* site);
+/* Text of the last CUDA runtime failure reported as BITNET_ERR_CUDA on the
+ * calling thread (the failing call, cudaGetErrorString, code). */
+const char* bitnet_last_cuda_error(void);
+
+/* ---- process-wide launch options (no reference counterpart: ttnn chooses
+ * program configs internally) -------------------------------------------- */
+/* Launch kernels with programmatic dependent launch (default 1). */
+int bitnet_set_pdl(int enable);
+/* Force the K split (cluster size, 1..8) of the tcgen05 path; 0 = automatic. */
+int bitnet_set_tc_split(int split);
+/* BITNET_PATH_AUTO uses the SIMT path for M <= m (0..8, default 4). */
+int bitnet_set_simt_max_m(int m);
+
+/* ---- sizes of caller-owned buffers ------------------------------------------ */
+/* Bytes of the device weight layout for an [N, K] ternary matrix
+ * (rows padded to 128, K padded to 64, 2 bits per weight). */
+size_t bitnet_packed_weight_bytes(int N, int K);
+/* Bytes of the int8 activation buffer for M tokens x K features (token tiles of
+ * at most 256 rows, K padded to 64).  row_scale / row_sum need bitnet_act_rows(M)
+ * entries each. */
+size_t bitnet_act_bytes(int M, int K);
+int bitnet_act_rows(int M);
+
+/* ---- weight packing (load time) -------------------------------------------
+ * Replaces the packed_ternary branch of Linear.load_weights /
+ * load_pretransposed_weight (src/bitnet_tt/layers/bitlinear.py:211-251, 269-298),
+ * which packs BFP2_b tiles for Tensix.  Input: int8 ternary codes W_q [N, K]
+ * row-major (values -1, 0, +1; anything else is treated as 0). */
+int bitnet_pack_ternary(const int8_t* w_q, int N, int K, uint8_t* w_packed, bitnet_stream_t stream);
+/* Same, from the repo's canonical 2-bit format produced by
+ * pack_ternary_weights (src/bitnet_tt/utils/quantization.py:111-138): the
+ * row-major [N, K] matrix flattened, 4 codes (w + 1) per byte, MSB first. */
+int bitnet_pack_from_canonical(const uint8_t* canonical, int N, int K, uint8_t* w_packed,
+                               bitnet_stream_t stream);
+
+/* ---- fused RMSNorm + per-token int8 absmax quantisation --------------------
+ * Replaces ttnn.rms_norm (src/bitnet_tt/layers/bitlinear.py:433-461) feeding
+ * the activation quantiser activation_quant_absmax
+ * (src/bitnet_tt/utils/quantization.py:60-91).
+ * x: bf16 [M, K] with row stride ldx elements.  gamma: bf16 [K] or NULL (no norm).
+ * q: int8 activation buffer (bitnet_act_bytes), row_scale[m] = 127 / absmax,
+ * row_sum[m] = sum_k q[m, k].  normed_out (nullable): the bf16 normalised rows
+ * [M, K] (contiguous).  q, row_scale and row_sum may all be NULL when only
+ * normed_out is wanted (plain RMSNorm). */
+int bitnet_act_quant(const void* x, int M, int K, int ldx, const void* gamma, float eps, int8_t* q,
+                     float* row_scale, int32_t* row_sum, void* normed_out, bitnet_stream_t stream);
+
+/* ---- BitLinear from quantised activations -----------------------------------
+ * Replaces ttnn.experimental.ternary_matmul(x, w, use_packed_ternary=True, ...)
+ * plus the post-scale of Linear.__call__ (src/bitnet_tt/layers/bitlinear.py:309-353,
+ * op call 336-341, scale 351-352) and the fused-projection epilogues of
+ * FeedForward.__call__ (src/bitnet_tt/layers/ffn.py:140-170) and the residual
+ * adds of the decode step (src/bitnet_tt/inference/generator_batch32.py:749, 756).
+ * acc[m, n] = sum_k q[m, k] * W[n, k] (int32, exact); y = bf16(acc * (scale_seg(n) / row_scale[m])).
+ * y: bf16 [M, N] ([M, N/2] for RELU2_MUL).  residual: bf16 [M, N] for RESIDUAL_ADD
+ * (may alias y).  acc_out (nullable): int32 [M, N] accumulators, for parity checks. */
+int bitnet_bitlinear_q(const int8_t* q, const float* row_scale, const int32_t* row_sum, int M, int K,
+                       const uint8_t* w_packed, int N, const bitnet_segments_t* segments, int epilogue,
+                       const void* residual, void* y, int32_t* acc_out, int path, bitnet_stream_t stream);
+
+/* ---- fused BitLinear (norm + quant + ternary matmul + epilogue) --------------
+ * bitnet_act_quant followed by bitnet_bitlinear_q; q_ws / scale_ws / sum_ws are
+ * the caller's activation buffers (bitnet_act_bytes / bitnet_act_rows).
+ * Replaces the fused-norm ternary_matmul call of the decode step
+ * (src/bitnet_tt/inference/generator_batch32.py:718-727). */
+int bitnet_bitlinear(const void* x, int M, int K, const void* gamma, float eps, const uint8_t* w_packed,
+                     int N, const bitnet_segments_t* segments, int epilogue, const void* residual, void* y,
+                     int32_t* acc_out, int8_t* q_ws, float* scale_ws, int32_t* sum_ws, int path,
+                     bitnet_stream_t stream);
+
+/* ---- GQA decode attention with fused RoPE and KV append --------------------
+ * Replaces nlp_create_qkv_heads_decode + rotary_embedding_llama +
+ * paged_update_cache + scaled_dot_product_attention_decode +
+ * nlp_concat_heads_decode (src/bitnet_tt/layers/attention.py:1040-1262).
+ * qkv: bf16 [B, (n_heads + 2*n_kv_heads) * head_dim] (Q | K | V, already scaled).
+ * positions: int32 [B], the position of the token being decoded per sequence.
+ * rope_cos / rope_sin: bf16 [rope_len, head_dim/2] (HF half-split convention).
+ * k_cache / v_cache: bf16 [B, n_kv_heads, max_len, head_dim]; row `positions[b]`
+ * is overwritten with the rotated K / V of this token.
+ * out: bf16 [B, n_heads * head_dim].  head_dim must be 128. */
+int bitnet_gqa_decode_attention(const void* qkv, int B, int n_heads, int n_kv_heads, int head_dim,
+                                const int32_t* positions, const void* rope_cos, const void* rope_sin,
+                                int rope_len, void* k_cache, void* v_cache, int max_len, float scale, void* out,
+                                bitnet_stream_t stream);
+
+/* ---- lm_head / embedding table -------------------------------------------
+ * The tied embedding / lm_head matrix (src/bitnet_tt/utils/weights.py:236-246)
+ * is stored once, in a tiled layout read by both the lm_head and the gather. */
+size_t bitnet_lm_head_bytes(int V, int K);
+int bitnet_pack_lm_head(const void* w, int V, int K, void* w_tiled, bitnet_stream_t stream);
+/* Embedding lookup (src/bitnet_tt/layers/embedding.py:14-70 and the host-side
+ * embed copy of src/bitnet_tt/inference/generator_batch32.py:981-1003):
+ * out[b, :] = W[ids[b], :], bf16 [B, K]. */
+int bitnet_embed_gather(const int32_t* ids, int B, const void* w_tiled, int V, int K, void* out,
+                        bitnet_stream_t stream);
+
+/* ---- lm_head with fused greedy argmax ---------------------------------------
+ * Replaces the lm_head matmul chunks + ttnn.argmax of the decode step
+ * (src/bitnet_tt/inference/generator_batch32.py:768-811, 1170-1174).
+ * h: bf16 [B, K] (already final-normed).  out_ids[b] = argmax_v bf16(h[b] . W[v])
+ * (first index on ties).  workspace: bitnet_argmax_workspace_bytes(B, V) bytes.
+ * logits_out (nullable): bf16 [B, V].  advance_positions (nullable): int32 [B],
+ * incremented by one after the ids are written (the next decode position). */
+size_t bitnet_argmax_workspace_bytes(int B, int V);
+int bitnet_lm_head_argmax(const void* h, int B, int K, const void* w_tiled, int V, void* workspace,
+                          int32_t* out_ids, void* logits_out, int32_t* advance_positions,
+                          bitnet_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BITNET_B200_H */

@@ -1,0 +1,65 @@
+"""The C-ABI library loads without a GPU and exports every entry point that
+include/bitnet_b200.h declares.  Only pure host helpers are called here."""
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from conftest import ROOT
+
+
+def header_functions() -> list[str]:
+    src = open(os.path.join(ROOT, "include", "bitnet_b200.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(bitnet_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_library_exports_every_declared_symbol():
+    from bitnet_tt import _lib
+
+    lib = _lib.load()
+    names = header_functions()
+    assert len(names) >= 20
+    missing = [n for n in names if not hasattr(lib, n)]
+    assert not missing, f"declared but not exported: {missing}"
+    # the Python binding declares a signature for every exported entry point
+    assert sorted(_lib.exported_symbols()) == names
+
+
+def test_status_strings_and_sizes():
+    from bitnet_tt import _lib
+
+    lib = _lib.load()
+    assert lib.bitnet_abi_version() == 1
+    assert _lib.status_string(0) == "ok"
+    assert "invalid argument" in _lib.status_string(-1)
+    assert "unknown" in _lib.status_string(-99)
+    # 2 bits per weight, rows padded to 128 and K to 64
+    assert _lib.packed_weight_bytes(6912, 2560) == 6912 * 2560 // 4
+    assert _lib.packed_weight_bytes(130, 70) == 256 * 128 // 4
+    assert _lib.act_rows(1) == 16 and _lib.act_rows(32) == 32 and _lib.act_rows(300) == 512
+    assert _lib.act_bytes(32, 2560) == 32 * 2560
+    assert _lib.lm_head_bytes(128256, 2560) == 128256 * 2560 * 2
+    assert _lib.argmax_workspace_bytes(32, 128256) == 1002 * 32 * 8
+    assert lib.bitnet_packed_weight_bytes(0, 5) == 0
+
+
+def test_option_validation_is_host_side():
+    from bitnet_tt import _lib
+
+    with pytest.raises(RuntimeError):
+        _lib.set_tc_split(9)
+    with pytest.raises(RuntimeError):
+        _lib.set_simt_max_m(-1)
+    _lib.set_tc_split(0)
+    _lib.set_simt_max_m(4)
+
+
+def test_library_is_sm100a_only():
+    """The .so carries sm_100a machine code (checked by its ELF note, not by disassembly)."""
+    from bitnet_tt import _lib
+
+    data = open(_lib.LIB_PATH, "rb").read()
+    assert b"sm_100a" in data

@@ -1,0 +1,193 @@
+"""GPU parity of the packing, quantisation and BitLinear kernels against the
+CPU oracle, through the C ABI.  Integer results (packed bytes, int8 codes,
+row sums, int32 accumulators) must be bit-exact; the bf16 outputs follow the
+oracle's rounding points and must match bit for bit as well."""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import bitlinear as ob
+from oracle import quant as oq
+
+pytestmark = pytest.mark.gpu
+
+
+def _lib():
+    from bitnet_tt import _lib as L
+
+    return L
+
+
+def rand_bf16(shape, seed, scale=1.0):
+    g = torch.Generator().manual_seed(seed)
+    return (torch.randn(shape, generator=g) * scale).to(torch.bfloat16)
+
+
+def rand_ternary(n, k, seed, p0=0.4):
+    rng = np.random.default_rng(seed)
+    return rng.choice(np.array([-1, 0, 1], np.int8), size=(n, k), p=[(1 - p0) / 2, p0, (1 - p0) / 2])
+
+
+def f32(t: torch.Tensor) -> np.ndarray:
+    return t.float().cpu().numpy()
+
+
+# ---------------------------------------------------------------------------
+# packing
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("n,k", [(128, 64), (130, 70), (3840, 2560), (64, 6912), (1, 1)])
+def test_pack_ternary_bytes(cuda, n, k):
+    L = _lib()
+    w = rand_ternary(n, k, seed=n * 7 + k)
+    dev = L.pack_ternary(torch.from_numpy(w).to(cuda))
+    np.testing.assert_array_equal(dev.cpu().numpy(), ob.device_pack(w))
+
+
+@pytest.mark.parametrize("n,k", [(128, 64), (5, 7), (256, 2560)])
+def test_pack_from_canonical_bytes(cuda, n, k):
+    L = _lib()
+    w = rand_ternary(n, k, seed=k)
+    canon = oq.pack_ternary_weights(w)
+    dev = L.pack_from_canonical(torch.from_numpy(canon).to(cuda), n, k)
+    np.testing.assert_array_equal(dev.cpu().numpy(), ob.device_pack(w))
+
+
+# ---------------------------------------------------------------------------
+# fused RMSNorm + int8 absmax quantisation
+# ---------------------------------------------------------------------------
+def run_act_quant(x: torch.Tensor, gamma: torch.Tensor | None, eps: float, cuda):
+    L = _lib()
+    m, k = x.shape
+    bufs = L.ActBuffers(m, k, cuda)
+    normed = torch.empty((m, k), dtype=torch.bfloat16, device=cuda)
+    L.act_quant(x.to(cuda), gamma.to(cuda) if gamma is not None else None, eps, bufs, normed_out=normed)
+    torch.cuda.synchronize()
+    q = ob.act_unlayout(bufs.q.cpu().numpy(), m, k)
+    return q, f32(bufs.row_scale)[:m], bufs.row_sum.cpu().numpy()[:m], f32(normed)
+
+
+@pytest.mark.parametrize("m,k", [(1, 64), (3, 100), (8, 2560), (32, 2560), (32, 6912), (40, 320), (300, 128)])
+@pytest.mark.parametrize("with_gamma", [True, False])
+def test_act_quant_bit_exact(cuda, m, k, with_gamma):
+    x = rand_bf16((m, k), seed=m * 1000 + k)
+    gamma = (1 + 0.1 * rand_bf16((k,), seed=k).float()).to(torch.bfloat16) if with_gamma else None
+    q, s, rsum, normed = run_act_quant(x, gamma, 1e-5, cuda)
+    ref = ob.bitlinear(f32(x), f32(gamma) if gamma is not None else None, 1e-5, np.zeros((1, k), np.int8))
+    np.testing.assert_array_equal(normed, ref["normed"])
+    np.testing.assert_array_equal(q, ref["q"])
+    np.testing.assert_array_equal(s, ref["s"])
+    np.testing.assert_array_equal(rsum, ref["row_sum"])
+
+
+def test_act_quant_edge_rows(cuda):
+    k = 96
+    x = np.zeros((5, k), np.float32)
+    x[1, :] = 1e4 * np.linspace(-1, 1, k)        # large values
+    x[2, 0] = 127.0                               # KAT: absmax 127 -> scale 1
+    x[2, 1:8] = [0.5, 1.5, 2.5, -0.5, -1.5, -2.5, 3.5]  # exact .5 ties
+    x[3, :] = 1e-30                               # below the 1e-5 absmax clamp
+    x[4, :] = np.linspace(-3, 3, k)
+    xt = torch.from_numpy(x).to(torch.bfloat16)
+    q, s, rsum, _ = run_act_quant(xt, None, 1e-5, cuda)
+    ref = ob.bitlinear(f32(xt), None, 1e-5, np.zeros((1, k), np.int8))
+    np.testing.assert_array_equal(q, ref["q"])
+    np.testing.assert_array_equal(s, ref["s"])
+    np.testing.assert_array_equal(rsum, ref["row_sum"])
+    assert s[2] == 1.0 and q[2, :8].tolist() == [127, 0, 2, 2, 0, -2, -2, 4]
+    assert not q[0].any() and not q[3].any()
+
+
+# ---------------------------------------------------------------------------
+# BitLinear
+# ---------------------------------------------------------------------------
+def run_bitlinear(cuda, x, gamma, w_q, ends=None, scales=None, epilogue="none", residual=None, path=0,
+                  eps=1e-5):
+    L = _lib()
+    m, k = x.shape
+    n = w_q.shape[0]
+    wp = L.pack_ternary(torch.from_numpy(w_q).to(cuda))
+    bufs = L.ActBuffers(m, k, cuda)
+    L.act_quant(x.to(cuda), gamma.to(cuda) if gamma is not None else None, eps, bufs)
+    epi = {"none": L.EPI_NONE, "relu2_mul": L.EPI_RELU2_MUL, "residual_add": L.EPI_RESIDUAL_ADD}[epilogue]
+    seg = L.Segments.make(ends or [n], scales or [1.0]) if epilogue != "relu2_mul" else L.Segments.make([n // 2, n], scales)
+    n_out = n // 2 if epilogue == "relu2_mul" else n
+    y = torch.empty((m, n_out), dtype=torch.bfloat16, device=cuda)
+    res = residual.to(cuda) if residual is not None else None
+    acc = torch.empty((m, n), dtype=torch.int32, device=cuda)
+    L.bitlinear_q(bufs, m, k, wp, n, seg, epi, res, y, acc_out=acc, path=path)
+    torch.cuda.synchronize()
+    st, site = L.last_device_status()
+    assert st == 0, f"device status {st} at site {site}"
+    return acc.cpu().numpy(), f32(y)
+
+
+def check_bitlinear(cuda, m, n, k, path, epilogue="none", seed=0, split=0):
+    L = _lib()
+    x = rand_bf16((m, k), seed=seed + 1)
+    gamma = (1 + 0.1 * rand_bf16((k,), seed=seed + 2).float()).to(torch.bfloat16)
+    w = rand_ternary(n, k, seed=seed + 3)
+    residual = rand_bf16((m, n), seed=seed + 4) if epilogue == "residual_add" else None
+    if epilogue == "relu2_mul":
+        ends, scales = None, [0.021, 0.017]
+    elif n >= 384 and n % 128 == 0:
+        ends, scales = [n - 256, n - 128, n], [0.02, 0.03, 0.015]  # QKV-like segments
+    else:
+        ends, scales = [n], [0.02]
+    L.set_tc_split(split)
+    try:
+        acc, y = run_bitlinear(cuda, x, gamma, w, ends, scales, epilogue, residual, path)
+    finally:
+        L.set_tc_split(0)
+    ref = ob.bitlinear(f32(x), f32(gamma), 1e-5, w, ends, scales, epilogue,
+                       f32(residual) if residual is not None else None)
+    np.testing.assert_array_equal(acc, ref["acc"])
+    np.testing.assert_array_equal(y, ref["y"])
+
+
+@pytest.mark.parametrize("m", [1, 2, 3, 4, 8])
+@pytest.mark.parametrize("n,k", [(128, 256), (130, 320), (384, 2560)])
+def test_bitlinear_simt(cuda, m, n, k):
+    check_bitlinear(cuda, m, n, k, path=1, seed=m + n + k)
+
+
+@pytest.mark.parametrize("m", [1, 8, 16, 17, 32, 64, 200, 300])
+@pytest.mark.parametrize("n,k", [(128, 256), (130, 320), (384, 2560)])
+def test_bitlinear_tcgen05(cuda, m, n, k):
+    check_bitlinear(cuda, m, n, k, path=2, seed=m * 3 + n + k)
+
+
+@pytest.mark.parametrize("split", [1, 2, 3, 4, 7, 8])
+def test_bitlinear_tcgen05_k_split(cuda, split):
+    check_bitlinear(cuda, 32, 256, 2560, path=2, seed=split, split=split)
+
+
+@pytest.mark.parametrize("path", [1, 2])
+@pytest.mark.parametrize("epilogue", ["relu2_mul", "residual_add"])
+@pytest.mark.parametrize("m", [1, 4, 32])
+def test_bitlinear_epilogues(cuda, path, epilogue, m):
+    if path == 1 and m > 8:
+        pytest.skip("SIMT path serves M <= 8")
+    check_bitlinear(cuda, m, 256, 640, path=path, epilogue=epilogue, seed=m + path)
+
+
+@pytest.mark.parametrize("path", [1, 2])
+def test_bitlinear_config0_full_size(cuda, path):
+    """x [32, 2560], W [6912, 2560] with P(0) = 0.4, scale 0.02."""
+    m = 32 if path == 2 else 8
+    check_bitlinear(cuda, m, 6912, 2560, path=path, seed=2026)
+
+
+def test_bitlinear_rejects_bad_arguments(cuda):
+    L = _lib()
+    w = torch.zeros(L.packed_weight_bytes(128, 64), dtype=torch.uint8, device=cuda)
+    bufs = L.ActBuffers(4, 64, cuda)
+    y = torch.empty((4, 128), dtype=torch.bfloat16, device=cuda)
+    with pytest.raises(RuntimeError, match="invalid argument"):
+        L.bitlinear_q(bufs, 4, 64, w, 128, None, 7, None, y)  # unknown epilogue
+    with pytest.raises(RuntimeError, match="invalid argument"):
+        L.bitlinear_q(bufs, 4, 64, w, 128, None, L.EPI_RESIDUAL_ADD, None, y)  # residual missing
+    with pytest.raises(RuntimeError, match="invalid argument"):
+        L.bitlinear_q(bufs, 9, 64, w, 128, None, L.EPI_NONE, None, y, path=L.PATH_SIMT)  # SIMT serves M <= 8
+    with pytest.raises(RuntimeError, match="invalid argument"):
+        L.bitlinear_q(bufs, 4, 64, w, 128, L.Segments.make([100], [1.0]), L.EPI_NONE, None, y)  # seg end != N
