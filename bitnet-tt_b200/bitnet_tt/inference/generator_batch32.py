@@ -1,0 +1,257 @@
+"""Batched greedy decoding with the whole decode step captured in a CUDA graph.
+
+Mirrors the reference's Batch32Generator (src/bitnet_tt/inference/generator_batch32.py:
+__init__ 494-591, _decode_step_batch32 656-811, _capture_trace 1115-1181,
+_execute_trace 1183-1195, generate_streaming 1597-1720).  Differences of
+substance:
+  * every row of the batch is a real sequence (the reference pads one user to
+    32 rows), each with its own decode position, so the lm_head + argmax run
+    on all rows;
+  * one decode step is 9 kernels per layer + 4 (embedding gather, final norm,
+    lm_head + argmax); its input (token ids) and position counters live on the
+    device, the argmax kernel writes the next ids in place and advances the
+    positions, so graph replays chain without host work;
+  * the prompt is consumed by the same graph, one token per replay
+    (prefill by decode), before the timed decode.
+"""
+
+from __future__ import annotations
+
+import time
+from dataclasses import dataclass, field
+from typing import Any, Iterator, Sequence
+
+import numpy as np
+import torch
+
+from .. import _lib
+from ..layers.attention import KVCache
+from ..utils.rope import half_split_tables
+
+PADDED_BATCH = 32
+
+
+@dataclass
+class GenerationStats:
+    """reference generator_batch32.py:104-145."""
+
+    prompt_tokens: int = 0
+    generated_tokens: int = 0
+    prefill_time: float = 0.0
+    decode_time: float = 0.0
+    step_times_ms: list[float] = field(default_factory=list)
+
+    @property
+    def ttft_ms(self) -> float:
+        return self.prefill_time * 1000.0
+
+    @property
+    def tokens_per_second(self) -> float:
+        return self.generated_tokens / self.decode_time if self.decode_time > 0 else 0.0
+
+    @property
+    def avg_ms_per_token(self) -> float:
+        return 1000.0 * self.decode_time / max(1, len(self.step_times_ms))
+
+
+class DecodeState:
+    """Persistent device buffers of one batch (the graph's fixed addresses)."""
+
+    def __init__(self, model, batch: int, max_seq_len: int):
+        cfg = model.config
+        dev = model.device
+        h, f = cfg.hidden_size, cfg.intermediate_size
+        qkv = (cfg.num_attention_heads + 2 * cfg.num_key_value_heads) * cfg.head_dim
+        self.batch, self.max_seq_len = batch, max_seq_len
+        self.ids = torch.zeros(batch, dtype=torch.int32, device=dev)
+        self.positions = torch.zeros(batch, dtype=torch.int32, device=dev)
+        self.hidden = torch.zeros((batch, h), dtype=torch.bfloat16, device=dev)
+        self.qkv = torch.zeros((batch, qkv), dtype=torch.bfloat16, device=dev)
+        self.attn = torch.zeros((batch, cfg.num_attention_heads * cfg.head_dim), dtype=torch.bfloat16, device=dev)
+        self.mid = torch.zeros((batch, f), dtype=torch.bfloat16, device=dev)
+        self.normed = torch.zeros((batch, h), dtype=torch.bfloat16, device=dev)
+        self.act_h = _lib.ActBuffers(batch, h, dev)
+        self.act_f = _lib.ActBuffers(batch, f, dev)
+        self.argmax_ws = torch.zeros(_lib.argmax_workspace_bytes(batch, cfg.vocab_size), dtype=torch.uint8,
+                                     device=dev)
+        self.caches = []
+        for _ in range(cfg.num_layers):
+            c = KVCache(max_seq_len, batch, cfg.num_key_value_heads, cfg.head_dim, dev)
+            c.preallocate()
+            self.caches.append(c)
+        cos, sin = half_split_tables(cfg.head_dim, max_seq_len, cfg.rope_theta)
+        self.rope_cos, self.rope_sin = cos.to(dev), sin.to(dev)
+        self.logits: torch.Tensor | None = None
+
+    def kv_bytes(self) -> int:
+        return sum(c.key_cache.numel() * 2 * 2 for c in self.caches)
+
+
+class Batch32Generator:
+    def __init__(self, model, tokenizer: Any = None, enable_trace: bool = True, batch_size: int = PADDED_BATCH,
+                 max_seq_len: int = 2048, keep_logits: bool = False) -> None:
+        self.model = model
+        self.device = model.device
+        self.config = model.config
+        self.tokenizer = tokenizer
+        self.enable_trace = enable_trace
+        self.batch_size = batch_size
+        self.max_seq_len = max_seq_len
+        self.keep_logits = keep_logits
+        self.state: DecodeState | None = None
+        self._graph: torch.cuda.CUDAGraph | None = None
+        self.launches_per_step = 9 * self.config.num_layers + 4
+        self.last_stats = GenerationStats()
+
+    # ---- state / graph -----------------------------------------------------
+    def _ensure_state(self) -> DecodeState:
+        if self.state is None:
+            self.state = DecodeState(self.model, self.batch_size, self.max_seq_len)
+            if self.keep_logits:
+                self.state.logits = torch.zeros((self.batch_size, self.config.vocab_size), dtype=torch.bfloat16,
+                                                device=self.device)
+        return self.state
+
+    def _decode_step(self) -> None:
+        """Enqueue one decode step on the current stream (graph-capturable)."""
+        st = self.state
+        m, cfg = self.model, self.config
+        b, eps = st.batch, cfg.rms_norm_eps
+        m.embed_tokens.gather_into(st.ids, st.hidden)
+        for layer, cache in zip(m.layers, st.caches):
+            attn = layer.self_attn
+            _lib.act_quant(st.hidden, layer.input_layernorm.weight, eps, st.act_h)
+            attn.qkv_proj.forward_into(st.act_h, b, st.qkv)
+            attn.decode_attention(st.qkv, st.positions, st.rope_cos, st.rope_sin, cache, st.attn)
+            _lib.act_quant(st.attn, attn.attn_sub_norm.weight, eps, st.act_h)
+            attn.o_proj.forward_into(st.act_h, b, st.hidden, residual=st.hidden)
+            _lib.act_quant(st.hidden, layer.post_attention_layernorm.weight, eps, st.act_h)
+            layer.mlp.gate_up_proj.forward_into(st.act_h, b, st.mid)
+            _lib.act_quant(st.mid, layer.mlp.ffn_sub_norm.weight, eps, st.act_f)
+            layer.mlp.down_proj.forward_into(st.act_f, b, st.hidden, residual=st.hidden)
+        _lib.rmsnorm(st.hidden, m.norm.weight, eps, st.normed)
+        m.lm_head_argmax(st.normed, st.argmax_ws, st.ids, st.logits, st.positions)
+
+    def _capture_trace(self) -> None:
+        """Warm every kernel once eagerly, then capture the step into a CUDA graph."""
+        st = self._ensure_state()
+        saved_ids, saved_pos = st.ids.clone(), st.positions.clone()
+        side = torch.cuda.Stream(device=self.device)
+        side.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(side):
+            self._decode_step()
+        torch.cuda.current_stream(self.device).wait_stream(side)
+        torch.cuda.synchronize(self.device)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self._decode_step()
+        torch.cuda.synchronize(self.device)
+        st.ids.copy_(saved_ids)
+        st.positions.copy_(saved_pos)
+        self._graph = g
+
+    def release_trace(self) -> None:
+        self._graph = None
+
+    def step(self) -> None:
+        """One decode step for the whole batch (graph replay or eager launches)."""
+        if self.enable_trace:
+            if self._graph is None:
+                self._capture_trace()
+            self._graph.replay()
+        else:
+            self._decode_step()
+
+    def warmup(self) -> None:
+        self._ensure_state()
+        if self.enable_trace and self._graph is None:
+            self._capture_trace()
+
+    # ---- prompt processing ---------------------------------------------------
+    def reset(self) -> None:
+        st = self._ensure_state()
+        st.positions.zero_()
+        st.ids.zero_()
+
+    def _prompts(self, input_ids) -> list[np.ndarray]:
+        if isinstance(input_ids, torch.Tensor):
+            input_ids = input_ids.cpu().numpy()
+        if isinstance(input_ids, np.ndarray) and input_ids.ndim == 2:
+            prompts = [np.asarray(r, dtype=np.int64) for r in input_ids]
+        else:
+            prompts = [np.asarray(p, dtype=np.int64).reshape(-1) for p in input_ids]
+        if len(prompts) != self.batch_size:
+            raise ValueError(f"{len(prompts)} prompts for a batch of {self.batch_size}")
+        if any(p.size == 0 for p in prompts):
+            raise ValueError("every prompt needs at least one token")
+        if any(int(p.min()) < 0 or int(p.max()) >= self.config.vocab_size for p in prompts):
+            raise ValueError("token id out of range")
+        return prompts
+
+    def prefill(self, input_ids) -> np.ndarray:
+        """Run every prompt token through the decode step (ragged prompts allowed).
+        Returns the prompt lengths; afterwards st.ids holds each sequence's first
+        generated token and st.positions its next position."""
+        prompts = self._prompts(input_ids)
+        lens = np.array([p.size for p in prompts])
+        if int(lens.max()) >= self.max_seq_len:
+            raise ValueError("prompt longer than the KV cache")
+        self.warmup()
+        self.reset()
+        st = self.state
+        lmax = int(lens.max())
+        table = np.zeros((lmax, self.batch_size), dtype=np.int32)
+        for b, p in enumerate(prompts):
+            table[: p.size, b] = p
+        table_d = torch.from_numpy(table).to(self.device)
+        lens_d = torch.from_numpy(lens.astype(np.int32)).to(self.device)
+        for t in range(lmax):
+            # a sequence whose prompt is exhausted keeps its generated token
+            st.ids.copy_(torch.where(lens_d > t, table_d[t], st.ids))
+            self.step()
+        return lens
+
+    # ---- generation ----------------------------------------------------------
+    def generate(self, input_ids, max_new_tokens: int = 128) -> np.ndarray:
+        """Greedy decode: returns [batch, max_new_tokens] token ids (equal-length prompts)."""
+        prompts = self._prompts(input_ids)
+        if len({p.size for p in prompts}) != 1:
+            raise ValueError("generate() takes equal-length prompts; use prefill() + decode() for ragged ones")
+        if prompts[0].size + max_new_tokens > self.max_seq_len:
+            raise ValueError("prompt + max_new_tokens exceeds the KV cache")
+        stats = GenerationStats(prompt_tokens=int(prompts[0].size) * self.batch_size)
+        torch.cuda.synchronize(self.device)
+        t0 = time.perf_counter()
+        self.prefill(prompts)
+        out = torch.empty((max_new_tokens, self.batch_size), dtype=torch.int32, device=self.device)
+        out[0].copy_(self.state.ids)
+        torch.cuda.synchronize(self.device)
+        t1 = time.perf_counter()
+        for i in range(1, max_new_tokens):
+            self.step()
+            out[i].copy_(self.state.ids)
+        torch.cuda.synchronize(self.device)
+        t2 = time.perf_counter()
+        stats.prefill_time, stats.decode_time = t1 - t0, t2 - t1
+        stats.generated_tokens = (max_new_tokens - 1) * self.batch_size
+        stats.step_times_ms = [1000.0 * (t2 - t1) / max(1, max_new_tokens - 1)] * max(0, max_new_tokens - 1)
+        self.last_stats = stats
+        return out.t().cpu().numpy()
+
+    def generate_streaming(self, input_ids, max_new_tokens: int = 128) -> Iterator[np.ndarray]:
+        """Yields each step's tokens [batch] on the host.  Every step copies the
+        step's input ids from pinned host memory to the device and reads the new
+        ids back (the reference's per-token H2D input copy and 4-byte readout,
+        generator_batch32.py:1063-1083, 1355-1367)."""
+        self.prefill(input_ids)
+        host_in = torch.empty(self.batch_size, dtype=torch.int32, pin_memory=True)
+        host_out = torch.empty(self.batch_size, dtype=torch.int32, pin_memory=True)
+        host_out.copy_(self.state.ids)
+        yield host_out.numpy().copy()
+        for _ in range(1, max_new_tokens):
+            host_in.copy_(host_out)
+            self.state.ids.copy_(host_in, non_blocking=True)
+            self.step()
+            host_out.copy_(self.state.ids, non_blocking=True)
+            torch.cuda.current_stream(self.device).synchronize()
+            yield host_out.numpy().copy()
