@@ -78,6 +78,11 @@ _SIGNATURES = {
         [_c_void_p, _c_int, _c_int, _c_void_p, _c_float, _c_void_p, _c_int, ctypes.POINTER(Segments), _c_int,
          _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_int, _c_void_p],
     ),
+    "bitnet_bitlinear_noalloc": (
+        _c_int,
+        [_c_void_p, _c_int, _c_int, _c_void_p, _c_float, _c_void_p, _c_int, ctypes.POINTER(Segments), _c_int,
+         _c_void_p, _c_void_p, _c_void_p, _c_int, _c_void_p],
+    ),
     "bitnet_gqa_decode_attention": (
         _c_int,
         [_c_void_p, _c_int, _c_int, _c_int, _c_int, _c_void_p, _c_void_p, _c_void_p, _c_int, _c_void_p, _c_void_p,

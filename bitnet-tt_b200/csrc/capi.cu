@@ -233,6 +233,8 @@ const char* bitnet_status_string(int status) {
     case BITNET_ERR_UNSUPPORTED_DEVICE: return "current CUDA device is not an sm_100 (B200) GPU";
     case BITNET_ERR_CUDA: return "CUDA runtime call failed";
     case BITNET_ERR_DEVICE_TIMEOUT: return "a kernel gave up a bounded wait on the device";
+    case BITNET_ERR_SCRATCH_LIMIT:
+      return "problem exceeds the static scratch of bitnet_bitlinear_noalloc (see BITNET_NOALLOC_MAX_*)";
     default: return "unknown status";
   }
 }
@@ -479,3 +481,75 @@ int bitnet_lm_head_argmax(const void* h, int B, int K, const void* w_tiled, int 
 }
 
 }  // extern "C"
+
+// ===========================================================================
+// BitLinear without any caller-provided scratch (bitnet_bitlinear_noalloc).
+//
+// For callers that cannot allocate device memory at the point of the call --
+// e.g. an FFI host (cgo, JNI, a C plugin) that holds no CUDA allocator of its
+// own, or code running where allocation is forbidden -- the int8 activations,
+// row scales and row sums of bitnet_bitlinear live in one file-scope device
+// array instead of in buffers the caller passes in.  The array is part of the
+// library image: every GPU that loads the library holds it until the process
+// exits.
+//
+// Limits: act_rows(M) <= BITNET_NOALLOC_MAX_ROWS and
+// act_rows(M) * round_up(K, 64) <= BITNET_NOALLOC_MAX_ACT_BYTES.
+// Nothing in the array has to start at zero: every call's quantisation kernel
+// writes all of it that the same call's BitLinear kernel reads.
+// All calls share the array, so two calls whose kernels overlap on the GPU
+// (different streams, or different host threads) race on it.
+// ===========================================================================
+namespace {
+
+constexpr size_t kNoallocQBytes = BITNET_NOALLOC_MAX_ACT_BYTES;
+constexpr int kNoallocRows = BITNET_NOALLOC_MAX_ROWS;
+constexpr size_t kNoallocScaleOff = kNoallocQBytes;
+constexpr size_t kNoallocSumOff = kNoallocScaleOff + (size_t)kNoallocRows * sizeof(float);
+constexpr size_t kNoallocBytes = kNoallocSumOff + (size_t)kNoallocRows * sizeof(int32_t);
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoallocBytes];
+
+// Device address of g_noalloc_scratch per device.  In host code the array's
+// name is only a host-side stand-in, so the address is looked up once per
+// device with that device current and the looked-up pointer is what the
+// kernels receive.
+unsigned char* g_noalloc_ptr[kMaxDevices] = {};
+std::mutex g_noalloc_mu;
+
+int noalloc_scratch(unsigned char** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return BITNET_ERR_INVALID_ARGUMENT;
+  if (g_noalloc_ptr[dev] == nullptr) {
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (g_noalloc_ptr[dev] == nullptr) {
+      void* p = nullptr;
+      e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_noalloc_scratch)");
+      g_noalloc_ptr[dev] = static_cast<unsigned char*>(p);
+    }
+  }
+  *out = g_noalloc_ptr[dev];
+  return BITNET_OK;
+}
+
+}  // namespace
+
+extern "C" int bitnet_bitlinear_noalloc(const void* x, int M, int K, const void* gamma, float eps,
+                                        const uint8_t* w_packed, int N, const bitnet_segments_t* segments,
+                                        int epilogue, const void* residual, void* y, int32_t* acc_out, int path,
+                                        bitnet_stream_t stream) {
+  if (M <= 0 || K <= 0) return BITNET_ERR_INVALID_ARGUMENT;
+  const int rows = act_rows_of(M);
+  if (rows > kNoallocRows || (size_t)rows * (size_t)round_up(K, 64) > kNoallocQBytes)
+    return BITNET_ERR_SCRATCH_LIMIT;
+  unsigned char* base = nullptr;
+  if (int e = noalloc_scratch(&base)) return e;
+  int8_t* q = reinterpret_cast<int8_t*>(base);
+  float* scale = reinterpret_cast<float*>(base + kNoallocScaleOff);
+  int32_t* sum = reinterpret_cast<int32_t*>(base + kNoallocSumOff);
+  return bitnet_bitlinear(x, M, K, gamma, eps, w_packed, N, segments, epilogue, residual, y, acc_out, q, scale, sum,
+                          path, stream);
+}

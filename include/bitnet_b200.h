@@ -34,6 +34,7 @@ typedef void* bitnet_stream_t; /* cudaStream_t */
 #define BITNET_ERR_UNSUPPORTED_DEVICE (-3) /* the current device is not sm_100             */
 #define BITNET_ERR_CUDA (-4)             /* a CUDA runtime call (launch, attribute) failed  */
 #define BITNET_ERR_DEVICE_TIMEOUT (-5)   /* a kernel gave up a bounded wait (see below)     */
+#define BITNET_ERR_SCRATCH_LIMIT (-6)    /* problem larger than bitnet_bitlinear_noalloc's static scratch */
 
 /* ---- BitLinear epilogues ------------------------------------------------ */
 #define BITNET_EPI_NONE 0          /* y = bf16(acc * w_scale / s_m)                                */
@@ -131,6 +132,27 @@ int bitnet_bitlinear(const void* x, int M, int K, const void* gamma, float eps, 
                      int N, const bitnet_segments_t* segments, int epilogue, const void* residual, void* y,
                      int32_t* acc_out, int8_t* q_ws, float* scale_ws, int32_t* sum_ws, int path,
                      bitnet_stream_t stream);
+
+/* ---- fused BitLinear without caller-provided scratch ------------------------
+ * No counterpart in the reference: an addition for callers that cannot
+ * allocate device memory where they call -- an FFI host (cgo, JNI, a C plugin)
+ * that holds no CUDA allocator, or code that runs where allocation is not
+ * allowed.  Same arguments and results as bitnet_bitlinear, minus q_ws /
+ * scale_ws / sum_ws: the int8 activations, row scales and row sums live in a
+ * static device array of the library (BITNET_NOALLOC_MAX_ACT_BYTES bytes plus
+ * 2 KB), held by every GPU that loads the library until the process exits.
+ * Calls with bitnet_act_rows(M) > BITNET_NOALLOC_MAX_ROWS or
+ * bitnet_act_rows(M) * round_up(K, 64) > BITNET_NOALLOC_MAX_ACT_BYTES return
+ * BITNET_ERR_SCRATCH_LIMIT.  The first call on a device looks up the array's
+ * device address (cudaGetSymbolAddress) and should therefore come before any
+ * stream capture on that device.  Every call shares the one array, so calls
+ * whose kernels overlap on the GPU (other streams, other host threads) race;
+ * serialise them.  No allocation happens inside. */
+#define BITNET_NOALLOC_MAX_ROWS 256
+#define BITNET_NOALLOC_MAX_ACT_BYTES (1u << 20)
+int bitnet_bitlinear_noalloc(const void* x, int M, int K, const void* gamma, float eps, const uint8_t* w_packed,
+                             int N, const bitnet_segments_t* segments, int epilogue, const void* residual, void* y,
+                             int32_t* acc_out, int path, bitnet_stream_t stream);
 
 /* ---- GQA decode attention with fused RoPE and KV append --------------------
  * Replaces nlp_create_qkv_heads_decode + rotary_embedding_llama +
