@@ -307,7 +307,7 @@ def kernel_rooflines(gen, args, hbm_peak: float) -> dict:
           kv_bytes + 2 * b * qkv_n + 2 * b * h, nl)
     ws = st.argmax_ws
     ids = torch.empty_like(st.ids)
-    entry("lm_head", lambda: m.lm_head_argmax(st.normed, ws, ids), 1, 2 * v * h + 2 * b * h, 1)
+    entry("lm_head", lambda: m.lm_head_argmax(st.normed, ws, ids), 1, 2 * v * h + 2 * b * h, 1)  # 3 launches
     st.positions.copy_(pos_save)
     torch.cuda.synchronize()
     return res
@@ -441,8 +441,8 @@ def run_b200(args) -> None:
 
 def gen_launches(cfg) -> int:
     """Kernels of one decode step: embedding gather; per layer 4 act-quant, 4
-    BitLinear, 1 attention; final norm, lm_head, argmax reduce."""
-    return 1 + 9 * cfg.num_layers + 3
+    BitLinear, 1 attention; final norm, hidden-state tiling, lm_head, argmax reduce."""
+    return 1 + 9 * cfg.num_layers + 4
 
 
 def main() -> None:

@@ -91,7 +91,7 @@ _SIGNATURES = {
     "bitnet_lm_head_bytes": (_c_size_t, [_c_int, _c_int]),
     "bitnet_pack_lm_head": (_c_int, [_c_void_p, _c_int, _c_int, _c_void_p, _c_void_p]),
     "bitnet_embed_gather": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_int, _c_int, _c_void_p, _c_void_p]),
-    "bitnet_argmax_workspace_bytes": (_c_size_t, [_c_int, _c_int]),
+    "bitnet_argmax_workspace_bytes": (_c_size_t, [_c_int, _c_int, _c_int]),
     "bitnet_lm_head_argmax": (
         _c_int,
         [_c_void_p, _c_int, _c_int, _c_void_p, _c_int, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p],
@@ -270,8 +270,8 @@ def embed_gather(ids: torch.Tensor, w_tiled: torch.Tensor, v: int, k: int, out: 
           "bitnet_embed_gather")
 
 
-def argmax_workspace_bytes(b: int, v: int) -> int:
-    return int(load().bitnet_argmax_workspace_bytes(b, v))
+def argmax_workspace_bytes(b: int, k: int, v: int) -> int:
+    return int(load().bitnet_argmax_workspace_bytes(b, k, v))
 
 
 def lm_head_argmax(h: torch.Tensor, w_tiled: torch.Tensor, v: int, workspace: torch.Tensor, out_ids: torch.Tensor,

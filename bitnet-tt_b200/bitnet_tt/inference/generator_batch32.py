@@ -72,7 +72,7 @@ class DecodeState:
         self.normed = torch.zeros((batch, h), dtype=torch.bfloat16, device=dev)
         self.act_h = _lib.ActBuffers(batch, h, dev)
         self.act_f = _lib.ActBuffers(batch, f, dev)
-        self.argmax_ws = torch.zeros(_lib.argmax_workspace_bytes(batch, cfg.vocab_size), dtype=torch.uint8,
+        self.argmax_ws = torch.zeros(_lib.argmax_workspace_bytes(batch, h, cfg.vocab_size), dtype=torch.uint8,
                                      device=dev)
         self.caches = []
         for _ in range(cfg.num_layers):
@@ -100,7 +100,7 @@ class Batch32Generator:
         self.keep_logits = keep_logits
         self.state: DecodeState | None = None
         self._graph: torch.cuda.CUDAGraph | None = None
-        self.launches_per_step = 9 * self.config.num_layers + 4
+        self.launches_per_step = 9 * self.config.num_layers + 5
         self.last_stats = GenerationStats()
 
     # ---- state / graph -----------------------------------------------------

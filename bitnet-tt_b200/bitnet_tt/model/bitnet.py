@@ -57,7 +57,7 @@ class BitNetModel:
             h = layer(h, positions, rope, cache)
         normed = self.norm(h)
         b = normed.shape[0]
-        ws = torch.empty(_lib.argmax_workspace_bytes(b, self.config.vocab_size), dtype=torch.uint8,
+        ws = torch.empty(_lib.argmax_workspace_bytes(b, self.config.hidden_size, self.config.vocab_size), dtype=torch.uint8,
                          device=self.device)
         nxt = torch.empty(b, dtype=torch.int32, device=self.device)
         logits = (torch.empty((b, self.config.vocab_size), dtype=torch.bfloat16, device=self.device)

@@ -19,6 +19,7 @@
 #include "bitlinear_tc.cuh"
 #include "common.cuh"
 #include "lm_head.cuh"
+#include "lm_head_tc.cuh"
 #include "pack.cuh"
 #include "../../include/bitnet_b200.h"
 
@@ -146,6 +147,9 @@ int to_dev_segments(const bitnet_segments_t* s, int N, int epilogue, bitnet_segm
 }
 
 std::atomic<unsigned long long> g_smem_aq{0}, g_smem_simt[3][4], g_smem_tc[3], g_smem_lmh{0};
+
+int lm_head_tile_T(int B) { return round_up(B, 16); }
+size_t lm_head_part_bytes(int B, int grid) { return (size_t)grid * B * sizeof(ArgPair); }
 
 template <int EPI, int MT>
 int launch_simt(const int8_t* q, const float* rs, const int32_t* rsum, int M, int Kp, int T, const uint8_t* w,
@@ -456,27 +460,52 @@ int bitnet_embed_gather(const int32_t* ids, int B, const void* w_tiled, int V, i
                 (const uint4*)w_tiled, V, K, KC8, (uint16_t*)out);
 }
 
-size_t bitnet_argmax_workspace_bytes(int B, int V) {
-  if (B <= 0 || V <= 0) return 0;
-  return (size_t)(round_up(V, 128) / 128) * (size_t)B * sizeof(ArgPair);
+// Workspace of bitnet_lm_head_argmax: the per-CTA (max, index) pairs
+// (<= kMaxLmGrid CTAs), then the hidden states in the tiled tcgen05 layout.
+constexpr int kMaxLmGrid = 160;
+static size_t lm_ws_hidden_offset(int B) { return (lm_head_part_bytes(B, kMaxLmGrid) + 255) / 256 * 256; }
+
+size_t bitnet_argmax_workspace_bytes(int B, int K, int V) {
+  if (B <= 0 || V <= 0 || K <= 0 || B > 256) return 0;
+  return lm_ws_hidden_offset(B) + (size_t)(round_up(K, 8) / 8) * lm_head_tile_T(B) * 16;
 }
 
 int bitnet_lm_head_argmax(const void* h, int B, int K, const void* w_tiled, int V, void* workspace, int32_t* out_ids,
                           void* logits_out, int32_t* advance_positions, bitnet_stream_t stream) {
   DevInfo* d;
   if (int e = device_info(&d)) return e;
-  if (!h || !w_tiled || !workspace || !out_ids || B <= 0 || B > LMH_TOK || V <= 0 || K <= 0)
+  if (!h || !w_tiled || !workspace || !out_ids || B <= 0 || B > 256 || V <= 0 || K <= 0 || (K % 16) != 0)
     return BITNET_ERR_INVALID_ARGUMENT;
-  if (!aligned(w_tiled, 16) || !aligned(workspace, 8) || !aligned(h, 2)) return BITNET_ERR_ALIGNMENT;
-  const int KC8 = round_up(K, 8) / 8, ntiles = round_up(V, 128) / 128;
-  const size_t smem = (size_t)KC8 * B * 16;
-  if (smem > kMaxDynSmem) return BITNET_ERR_INVALID_ARGUMENT;
-  if (int e = ensure_smem(lm_head_simt_kernel, &g_smem_lmh)) return e;
-  ArgPair* part = (ArgPair*)workspace;
-  if (int e = launch(lm_head_simt_kernel, dim3(ntiles), dim3(LMH_THREADS), smem, stream, 1, (const uint16_t*)h, B, K,
-                     (const uint4*)w_tiled, V, KC8, part, (uint16_t*)logits_out))
+  if (!aligned(w_tiled, 16) || !aligned(workspace, 256) || !aligned(h, 2)) return BITNET_ERR_ALIGNMENT;
+  const int K8 = round_up(K, 8) / 8, ntiles = round_up(V, 128) / 128, T = lm_head_tile_T(B);
+  const int grid = ntiles < d->sms ? ntiles : (d->sms < kMaxLmGrid ? d->sms : kMaxLmGrid);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  ArgPair* part = reinterpret_cast<ArgPair*>(ws);
+  uint8_t* h_tiled = ws + lm_ws_hidden_offset(B);
+  if (int e = launch(tile_hidden_kernel, dim3((K8 * T + 255) / 256), dim3(256), 0, stream, 1, (const uint16_t*)h, B,
+                     K, T, K8, reinterpret_cast<uint4*>(h_tiled)))
     return e;
-  return launch(argmax_reduce_kernel, dim3(B), dim3(256), 0, stream, 1, (const ArgPair*)part, ntiles, B, out_ids,
+  if (int e = ensure_smem(lm_head_tc_kernel, &g_smem_lmh)) return e;
+  const int slot = lmt_slot_bytes(T);
+  const int nstage_total = ((K8 + LMT_STAGE_CHUNKS - 1) / LMT_STAGE_CHUNKS) * ((ntiles + grid - 1) / grid);
+  int nslot = (int)((kMaxDynSmem - lmt_ctrl_bytes()) / slot);
+  if (nslot > LMT_MAX_SLOTS) nslot = LMT_MAX_SLOTS;
+  if (nslot > nstage_total) nslot = nstage_total;
+  if (nslot < 2) return BITNET_ERR_INVALID_ARGUMENT;
+  LmTcParams p;
+  p.w = (const uint8_t*)w_tiled;
+  p.h = h_tiled;
+  p.B = B;
+  p.T = T;
+  p.K8 = K8;
+  p.V = V;
+  p.ntiles = ntiles;
+  p.nslot = nslot;
+  p.part = part;
+  p.logits = (uint16_t*)logits_out;
+  const size_t smem = (size_t)lmt_ctrl_bytes() + (size_t)nslot * slot;
+  if (int e = launch(lm_head_tc_kernel, dim3(grid), dim3(LMT_THREADS), smem, stream, 1, p)) return e;
+  return launch(argmax_reduce_kernel, dim3(B), dim3(256), 0, stream, 1, (const ArgPair*)part, grid, B, out_ids,
                 advance_positions);
 }
 

@@ -184,10 +184,12 @@ int bitnet_embed_gather(const int32_t* ids, int B, const void* w_tiled, int V, i
  * Replaces the lm_head matmul chunks + ttnn.argmax of the decode step
  * (src/bitnet_tt/inference/generator_batch32.py:768-811, 1170-1174).
  * h: bf16 [B, K] (already final-normed).  out_ids[b] = argmax_v bf16(h[b] . W[v])
- * (first index on ties).  workspace: bitnet_argmax_workspace_bytes(B, V) bytes.
+ * (first index on ties); B <= 256.  workspace: bitnet_argmax_workspace_bytes(B, K, V)
+ * bytes, 256-byte aligned (per-CTA partial maxima + the hidden states re-tiled
+ * for the tensor cores).
  * logits_out (nullable): bf16 [B, V].  advance_positions (nullable): int32 [B],
  * incremented by one after the ids are written (the next decode position). */
-size_t bitnet_argmax_workspace_bytes(int B, int V);
+size_t bitnet_argmax_workspace_bytes(int B, int K, int V);
 int bitnet_lm_head_argmax(const void* h, int B, int K, const void* w_tiled, int V, void* workspace,
                           int32_t* out_ids, void* logits_out, int32_t* advance_positions,
                           bitnet_stream_t stream);

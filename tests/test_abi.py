@@ -42,7 +42,8 @@ def test_status_strings_and_sizes():
     assert _lib.act_rows(1) == 16 and _lib.act_rows(32) == 32 and _lib.act_rows(300) == 512
     assert _lib.act_bytes(32, 2560) == 32 * 2560
     assert _lib.lm_head_bytes(128256, 2560) == 128256 * 2560 * 2
-    assert _lib.argmax_workspace_bytes(32, 128256) == 1002 * 32 * 8
+    # per-CTA (max, idx) pairs for up to 160 CTAs, then the hidden states tiled (K x T bf16)
+    assert _lib.argmax_workspace_bytes(32, 2560, 128256) == 160 * 32 * 8 + 2560 * 32 * 2
     assert lib.bitnet_packed_weight_bytes(0, 5) == 0
 
 

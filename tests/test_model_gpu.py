@@ -86,7 +86,7 @@ def test_lm_head_argmax_and_embedding(cuda):
     _lib.embed_gather(ids, tiled, v, k, emb)
     np.testing.assert_array_equal(emb.cpu().view(torch.int16).numpy(), e[ids.cpu().long()].view(torch.int16).numpy())
 
-    ws = torch.empty(_lib.argmax_workspace_bytes(b, v), dtype=torch.uint8, device=cuda)
+    ws = torch.empty(_lib.argmax_workspace_bytes(b, k, v), dtype=torch.uint8, device=cuda)
     out = torch.empty(b, dtype=torch.int32, device=cuda)
     logits = torch.empty((b, v), dtype=torch.bfloat16, device=cuda)
     pos = torch.arange(b, dtype=torch.int32, device=cuda)
