@@ -48,6 +48,9 @@ act_quant_kernel(const uint16_t* __restrict__ x, int M, int K, int ldx, const ui
   __shared__ float red_f[32];
   __shared__ int red_i[32];
 
+  // Let the next kernel launch now (it waits for this grid to complete before
+  // it reads anything this grid writes); this grid waits for its predecessor.
+  pdl_trigger();
   pdl_wait();
   const int m = blockIdx.x;
   const int tid = threadIdx.x, nt = blockDim.x;
@@ -75,10 +78,7 @@ act_quant_kernel(const uint16_t* __restrict__ x, int M, int K, int ldx, const ui
   if (normed_out != nullptr && valid) {
     for (int k = tid; k < K; k += nt) normed_out[(size_t)m * K + k] = f32_to_bf16_bits(sval[k]);
   }
-  if (q == nullptr) {
-    pdl_trigger();
-    return;
-  }
+  if (q == nullptr) return;
 
   float amax = 0.f;
   for (int k = tid; k < K; k += nt) amax = fmaxf(amax, fabsf(sval[k]));
@@ -107,7 +107,6 @@ act_quant_kernel(const uint16_t* __restrict__ x, int M, int K, int ldx, const ui
     row_scale[m] = valid ? s : 1.0f;
     row_sum[m] = qsum;
   }
-  pdl_trigger();
 }
 
 }  // namespace bitnet

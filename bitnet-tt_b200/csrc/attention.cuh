@@ -44,6 +44,7 @@ __global__ void __launch_bounds__(ATT_THREADS) gqa_decode_kernel(const AttnParam
   __shared__ float sm_l[ATT_WARPS][G];
   __shared__ float sm_acc[ATT_WARPS][G][ATT_D];
 
+  pdl_trigger();  // the next kernel may launch; it waits for this grid before reading
   pdl_wait();
   const int b = blockIdx.x, g = blockIdx.y;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -162,7 +163,6 @@ __global__ void __launch_bounds__(ATT_THREADS) gqa_decode_kernel(const AttnParam
     for (int j = 0; j < 4; ++j) sm_acc[warp][hh][lane * 4 + j] = acc[hh][j];
   }
   __syncthreads();
-  pdl_trigger();
   for (int i = tid; i < G * ATT_D; i += ATT_THREADS) {
     const int hh = i / ATT_D, d = i % ATT_D;
     float M = -INFINITY;

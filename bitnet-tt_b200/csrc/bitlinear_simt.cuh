@@ -48,6 +48,7 @@ bitlinear_simt_kernel(const int8_t* __restrict__ q, const float* __restrict__ ro
 
   const uint8_t* wrow = w + wlayout_offset(n, 0, KC);
 
+  pdl_trigger();  // the next kernel may launch; it waits for this grid before reading
   pdl_wait();
   // Stage q rows 0..7 of the (single) token tile: for each 16-wide K chunk the
   // first core matrix (8 rows x 16 B) of the tile.
@@ -96,7 +97,6 @@ bitlinear_simt_kernel(const int8_t* __restrict__ q, const float* __restrict__ ro
 #pragma unroll
   for (int m = 0; m < MT; ++m) sred[(warp * MT + m) * 32 + lane] = acc[m];
   __syncthreads();
-  pdl_trigger();
 
   if (EPI == EPI_RELU2_MUL) {
     // pairs p (32) x tokens m: gate row n0 + p, up row n0 + 32 + p

@@ -14,13 +14,16 @@
 // Warp roles (416 threads):
 //   warps 0-7   unpackers: warp w owns TMEM lane quarter w % 4 and half of the
 //               four 64-wide K chunks of a stage; after tcgen05.wait::st each
-//               warp arrives on the A buffer's `a_full` barrier;
+//               warp arrives on the A buffer's `a_full` barrier.  A is a ring
+//               of up to 8 buffers (all of TMEM not taken by D): an MMA
+//               completes ~0.5-0.8 us after issue, so the unpackers must be
+//               able to run that far ahead;
 //   warps 8-11  MMA issuers: lane 0 of issuer i issues the stage's K steps
-//               kk = i, i+NACC, ... into its own accumulator D_i (several issuing
-//               threads keep the tensor core busy at small N, where one
-//               issuing thread alone is the bottleneck); each issuer commits
-//               to the A buffer's `a_empty`, the slot's `slot_free` and, at the
-//               end, `d_final`;
+//               kk = i, i+NACC, ... into its own accumulator D_i (more than
+//               one issuing thread: one thread alone issues at most one MMA
+//               per ~36 ns, too slow at small N); each issuer commits to the
+//               A buffer's `a_empty`, the slot's `slot_free` and, at the end,
+//               `d_final`;
 //   warp 12     producer: bulk copies of packed weights and activations into a
 //               ring of shared-memory slots (weights of the first slots before
 //               griddepcontrol.wait, so they overlap the previous kernel), the
@@ -43,8 +46,9 @@ constexpr int TC_THREADS = 13 * 32;
 constexpr int TC_EPI_THREADS = TC_UNPACK_WARPS * 32;
 constexpr int TC_STAGE_CHUNKS = 4;  // 4 x 64 = 256 K positions per stage
 constexpr int TC_MAX_SLOTS = 16;
-constexpr int TC_NBUF = 2;          // A buffers in TMEM (64 columns each)
-constexpr int TC_CTRL_BYTES = 3072;
+constexpr int TC_MAX_NBUF = 8;      // A buffers in TMEM (64 columns each)
+constexpr int TC_TMEM_COLS = 512;
+constexpr int TC_CTRL_BYTES = 5120;
 
 struct TcParams {
   const int8_t* q;
@@ -59,24 +63,28 @@ struct TcParams {
   int32_t* acc_out;
   int nslot;
   int split;
+  int nbuf;  // A buffers in TMEM
 };
 
 __host__ __device__ __forceinline__ int tc_slot_bytes(int T) { return TC_STAGE_CHUNKS * 2048 + TC_STAGE_CHUNKS * 64 * T; }
 __host__ __device__ __forceinline__ int tc_nacc(int T) { return T <= 32 ? 4 : (T <= 64 ? 2 : 1); }
-__host__ __device__ __forceinline__ int tc_tmem_cols(int T) {
-  return (TC_NBUF * 64 + tc_nacc(T) * T) <= 256 ? 256 : 512;
+__host__ __device__ __forceinline__ int tc_nbuf(int T) {
+  const int nb = (TC_TMEM_COLS - tc_nacc(T) * T) / 64;
+  return nb > TC_MAX_NBUF ? TC_MAX_NBUF : nb;
 }
 
 struct TcCtrl {
   uint64_t full[TC_MAX_SLOTS];
   uint64_t slot_free[TC_MAX_SLOTS];
-  uint64_t a_full[TC_NBUF];
-  uint64_t a_empty[TC_NBUF];
+  uint64_t a_full[TC_MAX_NBUF];
+  uint64_t a_empty[TC_MAX_NBUF];
   uint64_t d_final;
   uint32_t tmem_base;
   int abort_flag;
   float scale[256];  // row_scale of the tile's tokens
   int rsum[256];     // row_sum of the tile's tokens
+  float fac0[256];   // w_scale / row_scale per token (gate scale for RELU2_MUL)
+  float fac1[256];   // up scale / row_scale per token (RELU2_MUL)
 };
 
 template <int EPI>
@@ -87,13 +95,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1) bitlinear_tc_kernel(const TcPar
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int nb = blockIdx.x, mt = blockIdx.y, ks = blockIdx.z;
-  const int T = p.T, KC = p.KC, nslot = p.nslot, split = p.split;
+  const int T = p.T, KC = p.KC, nslot = p.nslot, split = p.split, NB = p.nbuf;
   const int NACC = tc_nacc(T);
   const int kc_begin = (ks * KC) / split, kc_end = ((ks + 1) * KC) / split;
   const int nstages = (kc_end - kc_begin + TC_STAGE_CHUNKS - 1) / TC_STAGE_CHUNKS;
+  // Every CTA of a launch reads the same activation block.  Starting each CTA
+  // at a different K stage spreads those reads over the L2 instead of having
+  // all SMs hit the same lines at once; the integer sum is order-independent.
+  const int rot = nstages > 0 ? (int)((blockIdx.x + blockIdx.y * 7u) % (unsigned)nstages) : 0;
   const int slot_bytes = tc_slot_bytes(T);
   const int wslot_bytes = TC_STAGE_CHUNKS * 2048;
-  const uint32_t ncols = tc_tmem_cols(T);
+  const uint32_t ncols = TC_TMEM_COLS;
   volatile int* abort_flag = &ctrl->abort_flag;
 
   if (tid == 0) {
@@ -101,7 +113,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) bitlinear_tc_kernel(const TcPar
       mbar_init(&ctrl->full[s], 1);
       mbar_init(&ctrl->slot_free[s], NACC);
     }
-    for (int b = 0; b < TC_NBUF; ++b) {
+    for (int b = 0; b < NB; ++b) {
       mbar_init(&ctrl->a_full[b], TC_UNPACK_WARPS);
       mbar_init(&ctrl->a_empty[b], NACC);
     }
@@ -119,10 +131,19 @@ __global__ void __launch_bounds__(TC_THREADS, 1) bitlinear_tc_kernel(const TcPar
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // The next kernel may launch now: its CTAs can start their own weight
+  // prefetch while this one runs; it waits for this grid before reading it.
+  pdl_trigger();
   const uint32_t tbase = ctrl->tmem_base;
-  const uint32_t tmem_d = tbase + TC_NBUF * 64;  // D_i at tmem_d + i * T
+  const uint32_t tmem_d = tbase + NB * 64;  // D_i at tmem_d + i * T
 
-  auto stage_chunks = [&](int s) { return min(TC_STAGE_CHUNKS, kc_end - (kc_begin + s * TC_STAGE_CHUNKS)); };
+  // logical stage s -> K chunks [kc0(s), kc0(s) + stage_chunks(s))
+  auto kc0 = [&](int s) {
+    int g = s + rot;
+    if (g >= nstages) g -= nstages;
+    return kc_begin + g * TC_STAGE_CHUNKS;
+  };
+  auto stage_chunks = [&](int s) { return min(TC_STAGE_CHUNKS, kc_end - kc0(s)); };
   auto wait = [&](uint64_t* bar, uint32_t parity, int site) -> bool {
     if (*abort_flag) return false;
     if (!mbar_wait(bar, parity, site)) {
@@ -131,40 +152,51 @@ __global__ void __launch_bounds__(TC_THREADS, 1) bitlinear_tc_kernel(const TcPar
     }
     return true;
   };
+  // on-chip hand-offs (A buffer full / empty): poll without suspending
+  auto wait_spin = [&](uint64_t* bar, uint32_t parity, int site) -> bool {
+    if (*abort_flag) return false;
+    if (!mbar_wait_spin(bar, parity, site)) {
+      *abort_flag = 1;
+      return false;
+    }
+    return true;
+  };
 
   if (warp == TC_PRODUCER_WARP) {
     // ------------------------------ producer ------------------------------
+    // A thread's bulk copies complete one after another (~0.3 us each), so the
+    // prologue spreads them over the lanes: lane s issues slot s.  Each lane
+    // only ever waits on barriers armed by other warps.
+    const int pre = min(nslot, nstages);
     int issued = 0;
-    if (lane == 0) {
-      const uint64_t policy = l2_policy_evict_first();
-      const int pre = min(nslot, nstages);
-      for (int s = 0; s < pre; ++s) {
-        const int nch = stage_chunks(s), kc_s = kc_begin + s * TC_STAGE_CHUNKS;
-        mbar_arrive_expect_tx(&ctrl->full[s], (uint32_t)(nch * 2048 + nch * 64 * T));
-        bulk_g2s_stream(ring + (size_t)s * slot_bytes, p.w + ((size_t)nb * KC + kc_s) * 2048u, nch * 2048,
-                        &ctrl->full[s], policy);
-      }
+    if (lane < pre) {
+      const int s = lane;
+      const int nch = stage_chunks(s), kc_s = kc0(s);
+      mbar_arrive_expect_tx(&ctrl->full[s], (uint32_t)(nch * 2048 + nch * 64 * T));
+      bulk_g2s_stream(ring + (size_t)s * slot_bytes, p.w + ((size_t)nb * KC + kc_s) * 2048u, nch * 2048,
+                      &ctrl->full[s], l2_policy_evict_first());
     }
     pdl_wait();
+    if (lane < pre) {
+      const int s = lane;
+      const int nch = stage_chunks(s), kc_s = kc0(s);
+      bulk_g2s(ring + (size_t)s * slot_bytes + wslot_bytes, p.q + (size_t)mt * T * p.Kp + (size_t)kc_s * 64 * T,
+               nch * 64 * T, &ctrl->full[s]);
+    }
     for (int i = lane; i < T; i += 32) {
       const int mg = mt * T + i;
       ctrl->scale[i] = p.row_scale[mg];
       ctrl->rsum[i] = p.row_sum[mg];
     }
     if (lane == 0) {
-      const int pre = min(nslot, nstages);
-      for (int s = 0; s < pre; ++s) {
-        const int nch = stage_chunks(s), kc_s = kc_begin + s * TC_STAGE_CHUNKS;
-        bulk_g2s(ring + (size_t)s * slot_bytes + wslot_bytes, p.q + (size_t)mt * T * p.Kp + (size_t)kc_s * 64 * T,
-                 nch * 64 * T, &ctrl->full[s]);
-      }
+      // Refills (only when the K range has more stages than the ring has slots).
       issued = pre;
       const uint64_t policy = l2_policy_evict_first();
       for (int s = pre; s < nstages; ++s) {
         const int slot = s % nslot;
         // the slot's previous stage (s - nslot) is fully consumed once its MMAs are done
         if (!wait(&ctrl->slot_free[slot], ((s / nslot) + 1) & 1, 200)) break;
-        const int nch = stage_chunks(s), kc_s = kc_begin + s * TC_STAGE_CHUNKS;
+        const int nch = stage_chunks(s), kc_s = kc0(s);
         mbar_arrive_expect_tx(&ctrl->full[slot], (uint32_t)(nch * 2048 + nch * 64 * T));
         bulk_g2s_stream(ring + (size_t)slot * slot_bytes, p.w + ((size_t)nb * KC + kc_s) * 2048u, nch * 2048,
                         &ctrl->full[slot], policy);
@@ -185,8 +217,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) bitlinear_tc_kernel(const TcPar
       const uint32_t d = tmem_d + iss * T;
       bool first = true;
       for (int s = 0; s < nstages; ++s) {
-        const int slot = s % nslot, b = s % TC_NBUF;
-        if (!wait(&ctrl->a_full[b], (s / TC_NBUF) & 1, 201)) break;
+        const int slot = s % nslot, b = s % NB;
+        if (!wait_spin(&ctrl->a_full[b], (s / NB) & 1, 201)) break;
         tc_fence_after();
         const uint32_t a_base = tbase + b * 64;
         const uint32_t b_base = smem_u32(ring + (size_t)slot * slot_bytes + wslot_bytes);
@@ -207,9 +239,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) bitlinear_tc_kernel(const TcPar
     const int quarter = warp & 3, half = warp >> 2;
     const int row = quarter * 32 + lane;
     for (int s = 0; s < nstages; ++s) {
-      const int slot = s % nslot, b = s % TC_NBUF;
+      const int slot = s % nslot, b = s % NB;
       bool ok = true;
-      if (s >= TC_NBUF) ok = wait(&ctrl->a_empty[b], ((s / TC_NBUF) + 1) & 1, 202);
+      if (s >= NB) ok = wait_spin(&ctrl->a_empty[b], ((s / NB) + 1) & 1, 202);
       if (ok) ok = wait(&ctrl->full[slot], (s / nslot) & 1, 203);
       if (ok) {
         const uint8_t* wsm = ring + (size_t)slot * slot_bytes;
@@ -238,7 +270,22 @@ __global__ void __launch_bounds__(TC_THREADS, 1) bitlinear_tc_kernel(const TcPar
   if (nstages > 0) wait(&ctrl->d_final, 0, 205);
   tc_fence_after();
   __syncthreads();  // scale / row-sum staging by the producer is visible too
-  pdl_trigger();
+  pdl_wait();       // (already satisfied) orders this thread's reads of residual after the predecessor
+
+  // Per-token scale factors, one IEEE division per token instead of one per
+  // output.  Valid when the tile's rows share one segment (always true for the
+  // fused QKV, whose segment ends are multiples of 128); otherwise the output
+  // loop divides per element.
+  const int N = p.N;
+  const int row_lo = nb * 128, row_hi = min(N, row_lo + 128) - 1;
+  const bool seg_uniform = (EPI == EPI_RELU2_MUL) || seg_scale_of(p.seg, row_lo) == seg_scale_of(p.seg, row_hi);
+  {
+    const float sc0 = (EPI == EPI_RELU2_MUL) ? p.seg.scale[0] : seg_scale_of(p.seg, row_lo);
+    for (int m = tid; m < T; m += TC_THREADS) {
+      ctrl->fac0[m] = __fdiv_rn(sc0, ctrl->scale[m]);
+      if (EPI == EPI_RELU2_MUL) ctrl->fac1[m] = __fdiv_rn(p.seg.scale[1], ctrl->scale[m]);
+    }
+  }
 
   // Partial D -> the owner of each token.  Rank j of the cluster owns tokens
   // [j * tok_cap, min(T, (j + 1) * tok_cap)).
@@ -289,50 +336,57 @@ __global__ void __launch_bounds__(TC_THREADS, 1) bitlinear_tc_kernel(const TcPar
 
   const bool aborted = *abort_flag != 0;
   const int m_begin = cr * tok_cap, m_end = min(T, m_begin + tok_cap);
-  const int N = p.N;
   if (!aborted && tid < TC_EPI_THREADS) {
     if (EPI == EPI_RELU2_MUL) {
       const int pr = tid & 63;   // pair within the tile
       const int part = tid >> 6; // four threads share a pair, splitting tokens
       const int g0 = (pr >> 5) * 64 + (pr & 31);  // gate row in tile; up row = g0 + 32
       const int ng = nb * 128 + g0, nu = ng + 32;
+      const bool row_ok = nu < N;
+      uint16_t* yb = p.y + nb * 64 + (g0 >> 6) * 32 + (g0 & 31);
+      const int* rg = recv + g0 * ldr - m_begin;
+      const int* ru = recv + (g0 + 32) * ldr - m_begin;
+      // Independent iterations: unrolled so their latency chains overlap.
+#pragma unroll 4
       for (int m = m_begin + part; m < m_end; m += 4) {
         const int mg = mt * T + m;
-        if (mg >= p.M || nu >= N) continue;
-        int ag = 0, au = 0;
+        int ag = -ctrl->rsum[m], au = ag;
         for (int j = 0; j < split; ++j) {
-          ag += recv[(j * 128 + g0) * ldr + (m - m_begin)];
-          au += recv[(j * 128 + g0 + 32) * ldr + (m - m_begin)];
+          ag += rg[j * 128 * ldr + m];
+          au += ru[j * 128 * ldr + m];
         }
-        const int rs = ctrl->rsum[m];
-        ag -= rs;
-        au -= rs;
-        if (p.acc_out) {
-          p.acc_out[(size_t)mg * N + ng] = ag;
-          p.acc_out[(size_t)mg * N + nu] = au;
+        const float g = round_bf16(__fmul_rn((float)ag, ctrl->fac0[m]));
+        const float u = round_bf16(__fmul_rn((float)au, ctrl->fac1[m]));
+        const uint16_t h = relu2_mul_bf16(g, u);
+        if (row_ok && mg < p.M) {
+          yb[(size_t)mg * (N >> 1)] = h;
+          if (p.acc_out) {
+            p.acc_out[(size_t)mg * N + ng] = ag;
+            p.acc_out[(size_t)mg * N + nu] = au;
+          }
         }
-        const float sm = ctrl->scale[m];
-        const float g = scaled_bf16(ag, p.seg.scale[0], sm);
-        const float u = scaled_bf16(au, p.seg.scale[1], sm);
-        p.y[(size_t)mg * (N >> 1) + nb * 64 + (g0 >> 6) * 32 + (g0 & 31)] = relu2_mul_bf16(g, u);
       }
     } else {
       const int row = tid & 127;
       const int part = tid >> 7;  // two threads share a row, splitting tokens
       const int n = nb * 128 + row;
       const float wsc = seg_scale_of(p.seg, n);
+      const bool row_ok = n < N;
+      const int* rr = recv + row * ldr - m_begin;
+#pragma unroll 4
       for (int m = m_begin + part; m < m_end; m += 2) {
         const int mg = mt * T + m;
-        if (mg >= p.M || n >= N) continue;
         int a = -ctrl->rsum[m];
-        for (int j = 0; j < split; ++j) a += recv[(j * 128 + row) * ldr + (m - m_begin)];
-        if (p.acc_out) p.acc_out[(size_t)mg * N + n] = a;
-        const float v = scaled_bf16(a, wsc, ctrl->scale[m]);
-        const size_t o = (size_t)mg * N + n;
-        if (EPI == EPI_RESIDUAL_ADD)
-          p.y[o] = residual_add_bf16(p.residual[o], v);
-        else
-          p.y[o] = f32_to_bf16_bits(v);
+        for (int j = 0; j < split; ++j) a += rr[j * 128 * ldr + m];
+        const float v = seg_uniform ? round_bf16(__fmul_rn((float)a, ctrl->fac0[m])) : scaled_bf16(a, wsc, ctrl->scale[m]);
+        if (row_ok && mg < p.M) {
+          const size_t o = (size_t)mg * N + n;
+          if (p.acc_out) p.acc_out[o] = a;
+          if (EPI == EPI_RESIDUAL_ADD)
+            p.y[o] = residual_add_bf16(p.residual[o], v);
+          else
+            p.y[o] = f32_to_bf16_bits(v);
+        }
       }
     }
   }

@@ -176,18 +176,61 @@ int dispatch_simt(const int8_t* q, const float* rs, const int32_t* rsum, int M, 
 
 // Shared-memory request of the tcgen05 BitLinear.  Besides the ring and the
 // epilogue buffers it has a floor that caps the number of resident CTAs per SM
-// to what tensor memory can serve at once (two 256-column CTAs, or one
-// 512-column CTA): every resident CTA then gets its columns immediately, so a
-// CTA of a cluster can never sit in tcgen05.alloc while its peers wait for it
-// at the cluster barrier.
+// at what tensor memory can serve at once (one CTA holding all 512 columns):
+// every resident CTA then gets its columns immediately, so a CTA of a cluster
+// can never sit in tcgen05.alloc while its peers wait for it at the cluster
+// barrier.
 size_t tc_smem_bytes(int T, int nslot, int split) {
   const size_t ring = (size_t)nslot * tc_slot_bytes(T);
   const size_t stage = (size_t)128 * (T + 1) * 4;
   const int tok_cap = (T + split - 1) / split;
   const size_t recv = (size_t)split * 128 * (tok_cap + 1) * 4;
   size_t bytes = TC_CTRL_BYTES + (split > 1 ? ring + recv : (ring > stage ? ring : stage));
-  const size_t floor_bytes = tc_tmem_cols(T) == 512 ? (size_t)116 * 1024 : (size_t)80 * 1024;
+  // every CTA takes all 512 TMEM columns: at most one resident CTA per SM
+  const size_t floor_bytes = (size_t)116 * 1024;
   return bytes < floor_bytes ? floor_bytes : bytes;
+}
+
+int tc_nslot(int T, int KC, int split) {
+  const int chunks_max = (KC + split - 1) / split;
+  const int stages_max = (chunks_max + TC_STAGE_CHUNKS - 1) / TC_STAGE_CHUNKS;
+  int nslot = TC_MAX_SLOTS;
+  if (nslot > stages_max) nslot = stages_max;
+  if (nslot < 2) nslot = 2;
+  while (nslot > 2 && tc_smem_bytes(T, nslot, split) > kMaxDynSmem) --nslot;
+  return nslot;
+}
+
+// Clusters of `split` CTAs that can be resident at once (cached per device, T, split).
+template <typename K>
+int tc_max_active_clusters(K kernel, int T, int split, const DevInfo& dev) {
+  static std::atomic<int> cache[kMaxDevices][9][17];  // [device][split][T/16]
+  int devid = 0;
+  cudaGetDevice(&devid);
+  const int ti = T / 16;
+  if (devid >= kMaxDevices || ti > 16) return 0;
+  int v = cache[devid][split][ti].load();
+  if (v != 0) return v - 1;
+  cudaLaunchConfig_t cfg;
+  memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = dim3(1, 1, split);
+  cfg.blockDim = dim3(TC_THREADS);
+  cfg.dynamicSmemBytes = tc_smem_bytes(T, tc_nslot(T, 64, split), split);
+  cudaLaunchAttribute at;
+  at.id = cudaLaunchAttributeClusterDimension;
+  at.val.clusterDim.x = 1;
+  at.val.clusterDim.y = 1;
+  at.val.clusterDim.z = (unsigned)split;
+  cfg.attrs = &at;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess) {
+    (void)cudaGetLastError();
+    n = 0;
+  }
+  (void)dev;
+  cache[devid][split][ti].store(n + 1);
+  return n;
 }
 
 template <int EPI>
@@ -199,25 +242,28 @@ int dispatch_tc(TcParams p, int ntile_n, int ntile_m, bitnet_stream_t st, const 
   if (split <= 0) {
     split = 1;
     if (ntile_m == 1 && p.T <= 64) {
-      split = dev.sms / tiles;
-      if (split > 8) split = 8;
+      int want = dev.sms / tiles;
+      if (want > 8) want = 8;
       const int by_k = p.KC / 4;  // at least one full 256-wide stage per CTA
-      if (split > by_k) split = by_k;
-      if (split < 1) split = 1;
+      if (want > by_k) want = by_k;
+      // Largest split whose clusters are all co-resident in one wave (cluster
+      // sizes that do not pack into the GPCs leave a second wave behind).
+      for (int sp = want; sp > 1; --sp) {
+        if (tc_max_active_clusters(k, p.T, sp, dev) >= tiles) {
+          split = sp;
+          break;
+        }
+      }
     }
   }
   if (split > 8 || split > p.KC) return BITNET_ERR_INVALID_ARGUMENT;
   if (split > 1 && p.T > 64) return BITNET_ERR_INVALID_ARGUMENT;
-  const int chunks_max = (p.KC + split - 1) / split;
-  const int stages_max = (chunks_max + TC_STAGE_CHUNKS - 1) / TC_STAGE_CHUNKS;
-  int nslot = TC_MAX_SLOTS;
-  if (nslot > stages_max) nslot = stages_max;
-  if (nslot < 2) nslot = 2;
-  while (nslot > 2 && tc_smem_bytes(p.T, nslot, split) > kMaxDynSmem) --nslot;
+  const int nslot = tc_nslot(p.T, p.KC, split);
   const size_t smem = tc_smem_bytes(p.T, nslot, split);
   if (smem > kMaxDynSmem) return BITNET_ERR_INVALID_ARGUMENT;
   p.nslot = nslot;
   p.split = split;
+  p.nbuf = tc_nbuf(p.T);
   return launch(k, dim3(ntile_n, ntile_m, split), dim3(TC_THREADS), smem, st, split, p);
 }
 

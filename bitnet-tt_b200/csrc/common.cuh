@@ -83,6 +83,30 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded busy-poll (non-suspending test_wait) for hand-offs that are expected
+// to complete within a microsecond; same contract as mbar_wait.
+__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, int site) {
+  if (mbar_test_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_test_wait(bar, parity)) {
+    if (clock64() - t0 > kSpinLimitCycles) {
+      record_error(DEV_ERR_TIMEOUT, site);
+      return false;
+    }
+  }
+  return true;
+}
 // Bounded wait for the phase with the given parity to complete.  Returns false
 // (and records the error) when the cycle budget runs out.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int site) {

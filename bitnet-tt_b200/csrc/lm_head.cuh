@@ -24,6 +24,7 @@ argmax_reduce_kernel(const ArgPair* __restrict__ part, int ntiles, int B, int32_
                      int32_t* __restrict__ positions) {
   __shared__ float sv[256];
   __shared__ int si[256];
+  pdl_trigger();
   pdl_wait();
   const int b = blockIdx.x, tid = threadIdx.x;
   float bv = -INFINITY;
@@ -49,7 +50,6 @@ argmax_reduce_kernel(const ArgPair* __restrict__ part, int ntiles, int B, int32_
     out_ids[b] = si[0];
     if (positions != nullptr) positions[b] += 1;
   }
-  pdl_trigger();
 }
 
 }  // namespace bitnet

@@ -26,6 +26,7 @@ namespace bitnet {
 constexpr int LMT_THREADS = 192;
 constexpr int LMT_STAGE_CHUNKS = 8;  // 8 x 8 bf16 = 64 K per stage
 constexpr int LMT_MAX_SLOTS = 12;
+constexpr int LMT_PRODUCERS = 4;
 
 struct LmTcParams {
   const uint8_t* w;      // tiled weights [V/128][K/8][128][8 bf16]
@@ -54,6 +55,7 @@ __host__ __device__ __forceinline__ int lmt_ctrl_bytes() { return (int)((sizeof(
 
 // Rearrange h [B, K] (bf16, row-major) into the tiled B-operand layout with T rows.
 __global__ void tile_hidden_kernel(const uint16_t* __restrict__ h, int B, int K, int T, int K8, uint4* __restrict__ out) {
+  pdl_trigger();
   pdl_wait();
   const int total = K8 * T;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
@@ -73,7 +75,6 @@ __global__ void tile_hidden_kernel(const uint16_t* __restrict__ h, int B, int K,
     // core matrix (c, m/8), row m%8
     out[((size_t)c * (T >> 3) + (m >> 3)) * 8 + (m & 7)] = v;
   }
-  pdl_trigger();
 }
 
 __global__ void __launch_bounds__(LMT_THREADS, 1) lm_head_tc_kernel(const LmTcParams p) {
@@ -107,6 +108,7 @@ __global__ void __launch_bounds__(LMT_THREADS, 1) lm_head_tc_kernel(const LmTcPa
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  pdl_trigger();
   const uint32_t tbase = ctrl->tmem_base;
 
   auto wait = [&](uint64_t* bar, uint32_t parity, int site) -> bool {
@@ -120,7 +122,13 @@ __global__ void __launch_bounds__(LMT_THREADS, 1) lm_head_tc_kernel(const LmTcPa
 
   if (warp == 4) {
     // ---------------- producer ----------------
-    if (lane == 0) {
+    // Lanes 0..nprod-1 each own the stages it = lane (mod nprod): a thread's
+    // bulk copies complete one after another, so a single producer thread
+    // cannot keep the ring full.  Each lane waits only on barriers armed by the
+    // MMA issuer (another warp), and nprod <= nslot, so a lane never waits for
+    // a slot whose previous stage belongs to a lane of the same round.
+    const int nprod = min(LMT_PRODUCERS, nslot);
+    if (lane < nprod) {
       const uint64_t policy = l2_policy_evict_first();
       const int total = my_tiles * nstage;
       auto stage_of = [&](int it, int& vt, int& c0, int& nch) {
@@ -131,7 +139,7 @@ __global__ void __launch_bounds__(LMT_THREADS, 1) lm_head_tc_kernel(const LmTcPa
       // The weights do not depend on the previous kernel: fill the ring's first
       // slots with them before waiting for the tiled hidden states.
       const int pre = min(nslot, total);
-      for (int it = 0; it < pre; ++it) {
+      for (int it = lane; it < pre; it += nprod) {
         int vt, c0, nch;
         stage_of(it, vt, c0, nch);
         mbar_arrive_expect_tx(&ctrl->full[it], (uint32_t)(nch * 2048 + nch * 16 * T));
@@ -139,14 +147,15 @@ __global__ void __launch_bounds__(LMT_THREADS, 1) lm_head_tc_kernel(const LmTcPa
                         &ctrl->full[it], policy);
       }
       pdl_wait();
-      for (int it = 0; it < pre; ++it) {
+      for (int it = lane; it < pre; it += nprod) {
         int vt, c0, nch;
         stage_of(it, vt, c0, nch);
         bulk_g2s(ring + (size_t)it * slot_bytes + LMT_STAGE_CHUNKS * 2048, p.h + (size_t)c0 * 16 * T, nch * 16 * T,
                  &ctrl->full[it]);
       }
-      int issued = pre;
-      for (int it = pre; it < total; ++it) {
+      int issued = -1;  // last stage this lane issued
+      if (lane < pre) issued = lane + ((pre - 1 - lane) / nprod) * nprod;
+      for (int it = pre + lane; it < total; it += nprod) {
         const int slot = it % nslot;
         if (!wait(&ctrl->empty[slot], ((it / nslot) + 1) & 1, 400)) break;
         int vt, c0, nch;
@@ -155,11 +164,15 @@ __global__ void __launch_bounds__(LMT_THREADS, 1) lm_head_tc_kernel(const LmTcPa
         mbar_arrive_expect_tx(&ctrl->full[slot], (uint32_t)(nch * 2048 + nch * 16 * T));
         bulk_g2s_stream(dst, p.w + ((size_t)vt * K8 + c0) * 2048, nch * 2048, &ctrl->full[slot], policy);
         bulk_g2s(dst + LMT_STAGE_CHUNKS * 2048, p.h + (size_t)c0 * 16 * T, nch * 16 * T, &ctrl->full[slot]);
-        issued = it + 1;
+        issued = it;
       }
       if (*abort_flag) {
-        // Let the copies still in flight land before the shared memory is released.
-        for (int it = max(0, issued - nslot); it < issued; ++it) mbar_wait(&ctrl->full[it % nslot], (it / nslot) & 1, 404);
+        // Let this lane's copies land before the shared memory is released.
+        // Older stages of the lane had their slot refilled, so they landed.
+        for (int it = max(0, issued - nslot + 1); it <= issued; ++it) {
+          const bool mine = (it < pre) ? (it % nprod == lane) : ((it - pre) % nprod == lane);
+          if (mine) mbar_wait(&ctrl->full[it % nslot], (it / nslot) & 1, 404);
+        }
       }
     }
   } else if (warp == 5) {
@@ -249,7 +262,6 @@ __global__ void __launch_bounds__(LMT_THREADS, 1) lm_head_tc_kernel(const LmTcPa
 
   tc_fence_before();
   __syncthreads();
-  pdl_trigger();
   if (warp == 0) {
     tc_fence_after();
     tmem_dealloc(tbase, ncols);

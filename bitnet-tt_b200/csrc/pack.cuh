@@ -110,6 +110,7 @@ __host__ __device__ __forceinline__ size_t lm_layout_offset16(int v, int c8, int
 // out[b, :] = table[ids[b], :] (bf16), one thread per 16-byte chunk.
 __global__ void embed_gather_kernel(const int32_t* __restrict__ ids, int B, const uint4* __restrict__ table,
                                     int V, int K, int KC8, uint16_t* __restrict__ out) {
+  pdl_trigger();
   pdl_wait();
   const int b = blockIdx.y;
   if (b >= B) return;
@@ -131,7 +132,6 @@ __global__ void embed_gather_kernel(const int32_t* __restrict__ ids, int B, cons
       for (int i = 0; i < 8 && k0 + i < K; ++i) dst[i] = e[i];
     }
   }
-  pdl_trigger();
 }
 
 }  // namespace bitnet
