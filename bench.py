@@ -303,7 +303,8 @@ def kernel_rooflines(gen, args, hbm_peak: float) -> dict:
     kv_bytes = int(b * ctx * cfg.num_key_value_heads * cfg.head_dim * 2 * 2)
     pos_save = st.positions.clone()
     entry("attention", lambda: [L.self_attn.decode_attention(st.qkv, st.positions, st.rope_cos, st.rope_sin, c,
-                                                              st.attn) for L, c in zip(m.layers, st.caches)], nl,
+                                                              st.attn, st.max_ctx, st.attn_ws)
+                                for L, c in zip(m.layers, st.caches)], nl,
           kv_bytes + 2 * b * qkv_n + 2 * b * h, nl)
     ws = st.argmax_ws
     ids = torch.empty_like(st.ids)
@@ -332,6 +333,7 @@ def run_b200(args) -> None:
 
     b = args.batch
     gen = Batch32Generator(model, batch_size=b, max_seq_len=args.max_seq_len)
+    gen.set_context_limit(args.prompt_len + args.new_tokens)  # positions cycle within it
     rng = np.random.default_rng(args.seed * 1000 + rank)
     prompts = rng.integers(0, cfg.vocab_size, size=(b, args.prompt_len))
     gen.prefill(prompts)

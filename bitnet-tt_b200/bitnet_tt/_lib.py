@@ -83,10 +83,11 @@ _SIGNATURES = {
         [_c_void_p, _c_int, _c_int, _c_void_p, _c_float, _c_void_p, _c_int, ctypes.POINTER(Segments), _c_int,
          _c_void_p, _c_void_p, _c_void_p, _c_int, _c_void_p],
     ),
+    "bitnet_gqa_decode_workspace_bytes": (_c_size_t, [_c_int, _c_int, _c_int, _c_int]),
     "bitnet_gqa_decode_attention": (
         _c_int,
         [_c_void_p, _c_int, _c_int, _c_int, _c_int, _c_void_p, _c_void_p, _c_void_p, _c_int, _c_void_p, _c_void_p,
-         _c_int, _c_float, _c_void_p, _c_void_p],
+         _c_int, _c_int, _c_float, _c_void_p, _c_size_t, _c_void_p, _c_void_p],
     ),
     "bitnet_lm_head_bytes": (_c_size_t, [_c_int, _c_int]),
     "bitnet_pack_lm_head": (_c_int, [_c_void_p, _c_int, _c_int, _c_void_p, _c_void_p]),
@@ -244,13 +245,26 @@ def bitlinear_q(bufs: ActBuffers, m: int, k: int, w_packed: torch.Tensor, n: int
           "bitnet_bitlinear_q")
 
 
+def gqa_decode_workspace_bytes(b: int, n_heads: int, n_kv: int, max_ctx: int) -> int:
+    return int(load().bitnet_gqa_decode_workspace_bytes(b, n_heads, n_kv, max_ctx))
+
+
+def gqa_decode_workspace(b: int, n_heads: int, n_kv: int, max_ctx: int, device) -> torch.Tensor | None:
+    """Zeroed attention workspace (None when the context needs no split)."""
+    nbytes = gqa_decode_workspace_bytes(b, n_heads, n_kv, max_ctx)
+    return torch.zeros(nbytes, dtype=torch.uint8, device=device) if nbytes > 0 else None
+
+
 def gqa_decode_attention(qkv: torch.Tensor, n_heads: int, n_kv: int, head_dim: int, positions: torch.Tensor,
                          rope_cos: torch.Tensor, rope_sin: torch.Tensor, k_cache: torch.Tensor,
-                         v_cache: torch.Tensor, scale: float, out: torch.Tensor) -> None:
+                         v_cache: torch.Tensor, scale: float, out: torch.Tensor, max_ctx: int = 0,
+                         workspace: torch.Tensor | None = None) -> None:
     b = qkv.shape[0]
+    ws_bytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
     check(load().bitnet_gqa_decode_attention(ptr(qkv), b, n_heads, n_kv, head_dim, ptr(positions), ptr(rope_cos),
                                              ptr(rope_sin), rope_cos.shape[0], ptr(k_cache), ptr(v_cache),
-                                             k_cache.shape[2], float(scale), ptr(out), stream_handle()),
+                                             k_cache.shape[2], int(max_ctx), float(scale), ptr(workspace), ws_bytes,
+                                             ptr(out), stream_handle()),
           "bitnet_gqa_decode_attention")
 
 

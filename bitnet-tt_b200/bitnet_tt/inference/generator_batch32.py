@@ -57,12 +57,16 @@ class GenerationStats:
 class DecodeState:
     """Persistent device buffers of one batch (the graph's fixed addresses)."""
 
-    def __init__(self, model, batch: int, max_seq_len: int):
+    def __init__(self, model, batch: int, max_seq_len: int, max_ctx: int = 0):
         cfg = model.config
         dev = model.device
         h, f = cfg.hidden_size, cfg.intermediate_size
         qkv = (cfg.num_attention_heads + 2 * cfg.num_key_value_heads) * cfg.head_dim
         self.batch, self.max_seq_len = batch, max_seq_len
+        # bound on positions + 1 baked into the captured attention launches
+        self.max_ctx = max_ctx or max_seq_len
+        self.attn_ws = _lib.gqa_decode_workspace(batch, cfg.num_attention_heads, cfg.num_key_value_heads,
+                                                 self.max_ctx, dev)
         self.ids = torch.zeros(batch, dtype=torch.int32, device=dev)
         self.positions = torch.zeros(batch, dtype=torch.int32, device=dev)
         self.hidden = torch.zeros((batch, h), dtype=torch.bfloat16, device=dev)
@@ -102,11 +106,26 @@ class Batch32Generator:
         self._graph: torch.cuda.CUDAGraph | None = None
         self.launches_per_step = 9 * self.config.num_layers + 5
         self.last_stats = GenerationStats()
+        self.context_limit = max_seq_len
+
+    def set_context_limit(self, n: int) -> None:
+        """Bound the positions the next steps reach (positions + 1 <= n).  The
+        attention splits the context in blocks of 256 keys, so the limit is
+        rounded up to that; a new limit re-captures the decode graph."""
+        n = min(self.max_seq_len, max(1, -(-int(n) // 256) * 256))
+        if n != self.context_limit:
+            self.context_limit = n
+            self._graph = None
+            if self.state is not None:
+                st = self.state
+                st.max_ctx = n
+                st.attn_ws = _lib.gqa_decode_workspace(self.batch_size, self.config.num_attention_heads,
+                                                       self.config.num_key_value_heads, n, self.device)
 
     # ---- state / graph -----------------------------------------------------
     def _ensure_state(self) -> DecodeState:
         if self.state is None:
-            self.state = DecodeState(self.model, self.batch_size, self.max_seq_len)
+            self.state = DecodeState(self.model, self.batch_size, self.max_seq_len, self.context_limit)
             if self.keep_logits:
                 self.state.logits = torch.zeros((self.batch_size, self.config.vocab_size), dtype=torch.bfloat16,
                                                 device=self.device)
@@ -122,7 +141,8 @@ class Batch32Generator:
             attn = layer.self_attn
             _lib.act_quant(st.hidden, layer.input_layernorm.weight, eps, st.act_h)
             attn.qkv_proj.forward_into(st.act_h, b, st.qkv)
-            attn.decode_attention(st.qkv, st.positions, st.rope_cos, st.rope_sin, cache, st.attn)
+            attn.decode_attention(st.qkv, st.positions, st.rope_cos, st.rope_sin, cache, st.attn, st.max_ctx,
+                                  st.attn_ws)
             _lib.act_quant(st.attn, attn.attn_sub_norm.weight, eps, st.act_h)
             attn.o_proj.forward_into(st.act_h, b, st.hidden, residual=st.hidden)
             _lib.act_quant(st.hidden, layer.post_attention_layernorm.weight, eps, st.act_h)
@@ -196,6 +216,8 @@ class Batch32Generator:
         lens = np.array([p.size for p in prompts])
         if int(lens.max()) >= self.max_seq_len:
             raise ValueError("prompt longer than the KV cache")
+        if int(lens.max()) > self.context_limit:
+            self.set_context_limit(int(lens.max()))
         self.warmup()
         self.reset()
         st = self.state
@@ -220,6 +242,7 @@ class Batch32Generator:
         if prompts[0].size + max_new_tokens > self.max_seq_len:
             raise ValueError("prompt + max_new_tokens exceeds the KV cache")
         stats = GenerationStats(prompt_tokens=int(prompts[0].size) * self.batch_size)
+        self.set_context_limit(prompts[0].size + max_new_tokens)
         torch.cuda.synchronize(self.device)
         t0 = time.perf_counter()
         self.prefill(prompts)
@@ -243,7 +266,9 @@ class Batch32Generator:
         step's input ids from pinned host memory to the device and reads the new
         ids back (the reference's per-token H2D input copy and 4-byte readout,
         generator_batch32.py:1063-1083, 1355-1367)."""
-        self.prefill(input_ids)
+        prompts = self._prompts(input_ids)
+        self.set_context_limit(max(p.size for p in prompts) + max_new_tokens)
+        self.prefill(prompts)
         host_in = torch.empty(self.batch_size, dtype=torch.int32, pin_memory=True)
         host_out = torch.empty(self.batch_size, dtype=torch.int32, pin_memory=True)
         host_out.copy_(self.state.ids)

@@ -63,6 +63,19 @@ class KVCache:
     def reset(self) -> None:
         self.seq_len_cached = 0
 
+    def attention_workspace(self, num_heads: int, max_ctx: int = 0) -> torch.Tensor | None:
+        """Zeroed split-context workspace of the decode attention kernel (None
+        when max_ctx needs no split); cached per size, the kernel leaves it zeroed."""
+        max_ctx = max_ctx or self.max_seq_len
+        nbytes = _lib.gqa_decode_workspace_bytes(self.batch_size, num_heads, self.num_kv_heads, max_ctx)
+        if nbytes == 0:
+            return None
+        ws = getattr(self, "_attn_ws", None)
+        if ws is None or ws.numel() < nbytes:
+            ws = torch.zeros(nbytes, dtype=torch.uint8, device=self.device)
+            self._attn_ws = ws
+        return ws
+
     def clear(self) -> None:
         self.key_cache = None
         self.value_cache = None
@@ -104,10 +117,14 @@ class MultiHeadAttention:
             self.attn_sub_norm.load_weights(attn_sub_norm_weight)
 
     def decode_attention(self, qkv: torch.Tensor, positions: torch.Tensor, rope_cos: torch.Tensor,
-                         rope_sin: torch.Tensor, cache: KVCache, out: torch.Tensor) -> None:
-        """RoPE + KV append + GQA attention for one token per sequence."""
+                         rope_sin: torch.Tensor, cache: KVCache, out: torch.Tensor, max_ctx: int = 0,
+                         workspace: torch.Tensor | None = None) -> None:
+        """RoPE + KV append + GQA attention for one token per sequence.  max_ctx
+        bounds positions + 1 (0: the cache length) and sets the context split."""
+        if workspace is None:
+            workspace = cache.attention_workspace(self.num_heads, max_ctx)
         _lib.gqa_decode_attention(qkv, self.num_heads, self.num_kv_heads, self.head_dim, positions, rope_cos,
-                                  rope_sin, cache.key_cache, cache.value_cache, self.scale, out)
+                                  rope_sin, cache.key_cache, cache.value_cache, self.scale, out, max_ctx, workspace)
 
     def __call__(self, hidden_states: torch.Tensor, positions: torch.Tensor, rope: tuple[torch.Tensor, torch.Tensor],
                  cache: KVCache, norm_weight: torch.Tensor | None = None, norm_epsilon: float = 1e-5,

@@ -109,4 +109,124 @@ act_quant_kernel(const uint16_t* __restrict__ x, int M, int K, int ldx, const ui
   }
 }
 
+// Fast path: K % 8 == 0, 16-byte aligned rows (ldx % 8 == 0) and gamma, and
+// K <= 8 * 256 * AQ_MAXC.  Each thread keeps up to AQ_MAXC 8-element chunks in
+// registers (16-byte loads; gamma is read before griddepcontrol.wait, since it
+// does not come from the previous kernel), and the three reductions use one
+// barrier each.  Same results as act_quant_kernel (the fp64 sum of squares is
+// exact in any order; max and the integer sum are order-free).
+constexpr int AQ_THREADS = 256;
+constexpr int AQ_MAXC = 4;
+
+__device__ __forceinline__ void aq_unpack8(const uint4 v, float* f) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    f[2 * e] = __uint_as_float(w[e] << 16);
+    f[2 * e + 1] = __uint_as_float(w[e] & 0xFFFF0000u);
+  }
+}
+
+template <typename T, typename Op>
+__device__ __forceinline__ T block_allreduce_once(T v, T* scratch, Op op) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = op(v, __shfl_xor_sync(0xffffffffu, v, o));
+  if (lane == 0) scratch[warp] = v;
+  __syncthreads();
+  T r = scratch[0];
+#pragma unroll
+  for (int i = 1; i < AQ_THREADS / 32; ++i) r = op(r, scratch[i]);
+  return r;
+}
+
+__global__ void __launch_bounds__(AQ_THREADS)
+act_quant_vec_kernel(const uint16_t* __restrict__ x, int M, int K, int ldx, const uint16_t* __restrict__ gamma,
+                     float eps, int8_t* __restrict__ q, float* __restrict__ row_scale, int32_t* __restrict__ row_sum,
+                     uint16_t* __restrict__ normed_out, int T, int Kp) {
+  __shared__ double red_d[AQ_THREADS / 32];
+  __shared__ float red_f[AQ_THREADS / 32];
+  __shared__ int red_i[AQ_THREADS / 32];
+  pdl_trigger();
+  const int m = blockIdx.x, tid = threadIdx.x;
+  const bool valid = m < M;
+  const int KC8 = K >> 3;  // chunks of 8
+  float gm[AQ_MAXC][8];
+#pragma unroll
+  for (int c = 0; c < AQ_MAXC; ++c) {
+    const int ch = tid + c * AQ_THREADS;
+    if (gamma != nullptr && ch < KC8) aq_unpack8(reinterpret_cast<const uint4*>(gamma)[ch], gm[c]);
+  }
+  pdl_wait();
+  float v[AQ_MAXC][8];
+  double ss = 0.0;
+#pragma unroll
+  for (int c = 0; c < AQ_MAXC; ++c) {
+    const int ch = tid + c * AQ_THREADS;
+    if (valid && ch < KC8) {
+      aq_unpack8(reinterpret_cast<const uint4*>(x + (size_t)m * ldx)[ch], v[c]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[c][e] = 0.f;
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) ss = fma((double)v[c][e], (double)v[c][e], ss);
+  }
+  if (gamma != nullptr) {
+    ss = block_allreduce_once(ss, red_d, OpAddD());
+    const float var = __double2float_rn(__ddiv_rn(ss, (double)K));
+    const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+#pragma unroll
+    for (int c = 0; c < AQ_MAXC; ++c)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[c][e] = round_bf16(__fmul_rn(gm[c][e], round_bf16(__fmul_rn(v[c][e], r))));
+  }
+  if (normed_out != nullptr && valid) {
+#pragma unroll
+    for (int c = 0; c < AQ_MAXC; ++c) {
+      const int ch = tid + c * AQ_THREADS;
+      if (ch < KC8) {
+        uint4 o;
+        o.x = (uint32_t)f32_to_bf16_bits(v[c][0]) | ((uint32_t)f32_to_bf16_bits(v[c][1]) << 16);
+        o.y = (uint32_t)f32_to_bf16_bits(v[c][2]) | ((uint32_t)f32_to_bf16_bits(v[c][3]) << 16);
+        o.z = (uint32_t)f32_to_bf16_bits(v[c][4]) | ((uint32_t)f32_to_bf16_bits(v[c][5]) << 16);
+        o.w = (uint32_t)f32_to_bf16_bits(v[c][6]) | ((uint32_t)f32_to_bf16_bits(v[c][7]) << 16);
+        reinterpret_cast<uint4*>(normed_out + (size_t)m * K)[ch] = o;
+      }
+    }
+  }
+  if (q == nullptr) return;
+  float amax = 0.f;
+#pragma unroll
+  for (int c = 0; c < AQ_MAXC; ++c)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(v[c][e]));
+  amax = fmaxf(block_allreduce_once(amax, red_f, OpMaxF()), 1e-5f);
+  const float s = __fdiv_rn(127.0f, amax);
+  int qsum = 0;
+#pragma unroll
+  for (int c = 0; c < AQ_MAXC; ++c) {
+    const int ch = tid + c * AQ_THREADS;
+    if (ch * 8 < Kp) {  // chunks past K (up to Kp) are written as zeros
+      uint32_t lo = 0, hi = 0;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        int qi = 0;
+        if (valid && ch < KC8) qi = max(-128, min(127, __float2int_rn(__fmul_rn(v[c][e], s))));
+        qsum += qi;
+        if (e < 4)
+          lo |= ((uint32_t)(qi & 0xFF)) << (8 * e);
+        else
+          hi |= ((uint32_t)(qi & 0xFF)) << (8 * (e - 4));
+      }
+      *reinterpret_cast<uint2*>(q + alayout_offset(m, ch * 8, T, Kp)) = make_uint2(lo, hi);
+    }
+  }
+  qsum = block_allreduce_once(qsum, red_i, OpAddI());
+  if (tid == 0) {
+    row_scale[m] = valid ? s : 1.0f;
+    row_sum[m] = qsum;
+  }
+}
+
 }  // namespace bitnet

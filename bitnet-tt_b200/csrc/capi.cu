@@ -27,7 +27,7 @@ using namespace bitnet;
 
 namespace {
 
-constexpr int kAbiVersion = 1;
+constexpr int kAbiVersion = 2;
 constexpr int kMaxDevices = 64;
 constexpr size_t kMaxDynSmem = 232448;  // 227 KB, the sm_100 per-CTA opt-in limit
 
@@ -146,7 +146,7 @@ int to_dev_segments(const bitnet_segments_t* s, int N, int epilogue, bitnet_segm
   return s->end[s->count - 1] == N ? BITNET_OK : BITNET_ERR_INVALID_ARGUMENT;
 }
 
-std::atomic<unsigned long long> g_smem_aq{0}, g_smem_simt[3][4], g_smem_tc[3], g_smem_lmh{0};
+std::atomic<unsigned long long> g_smem_aq{0}, g_smem_simt[3][4], g_smem_tc[3], g_smem_lmh{0}, g_smem_att[4];
 
 int lm_head_tile_T(int B) { return round_up(B, 16); }
 size_t lm_head_part_bytes(int B, int grid) { return (size_t)grid * B * sizeof(ArgPair); }
@@ -374,10 +374,14 @@ int bitnet_act_quant(const void* x, int M, int K, int ldx, const void* gamma, fl
     return BITNET_ERR_ALIGNMENT;
   if (q && !aligned(q, 16)) return BITNET_ERR_ALIGNMENT;
   const int Kp = round_up(K, 64);
+  const int rows = want_q ? act_rows_of(M) : M;
+  if (K % 8 == 0 && ldx % 8 == 0 && Kp <= 8 * AQ_THREADS * AQ_MAXC && aligned(x, 16) &&
+      (!gamma || aligned(gamma, 16)) && (!normed_out || aligned(normed_out, 16)))
+    return launch(act_quant_vec_kernel, dim3(rows), dim3(AQ_THREADS), 0, stream, 1, (const uint16_t*)x, M, K, ldx,
+                  (const uint16_t*)gamma, eps, q, row_scale, row_sum, (uint16_t*)normed_out, act_tile_of(M), Kp);
   const size_t smem = (size_t)Kp * 4;
   if (smem > kMaxDynSmem) return BITNET_ERR_INVALID_ARGUMENT;
   if (int e = ensure_smem(act_quant_kernel, &g_smem_aq)) return e;
-  const int rows = want_q ? act_rows_of(M) : M;
   return launch(act_quant_kernel, dim3(rows), dim3(256), smem, stream, 1, (const uint16_t*)x, M, K, ldx,
                 (const uint16_t*)gamma, eps, q, row_scale, row_sum, (uint16_t*)normed_out, act_tile_of(M), Kp);
 }
@@ -442,18 +446,33 @@ int bitnet_bitlinear(const void* x, int M, int K, const void* gamma, float eps, 
                             path, stream);
 }
 
+static int att_nsplit(int max_ctx) { return (max_ctx + ATT_SPLIT_KEYS - 1) / ATT_SPLIT_KEYS; }
+
+size_t bitnet_gqa_decode_workspace_bytes(int B, int n_heads, int n_kv_heads, int max_ctx) {
+  if (B <= 0 || n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads != 0 || max_ctx <= 0) return 0;
+  const int S = att_nsplit(max_ctx);
+  if (S <= 1) return 0;
+  const size_t counters = ((size_t)B * n_kv_heads * sizeof(int) + 255) / 256 * 256;
+  return counters + (size_t)B * n_kv_heads * S * att_part_floats(n_heads / n_kv_heads) * sizeof(float);
+}
+
 int bitnet_gqa_decode_attention(const void* qkv, int B, int n_heads, int n_kv_heads, int head_dim,
                                 const int32_t* positions, const void* rope_cos, const void* rope_sin, int rope_len,
-                                void* k_cache, void* v_cache, int max_len, float scale, void* out,
-                                bitnet_stream_t stream) {
+                                void* k_cache, void* v_cache, int max_len, int max_ctx, float scale, void* workspace,
+                                size_t workspace_bytes, void* out, bitnet_stream_t stream) {
   DevInfo* d;
   if (int e = device_info(&d)) return e;
   if (!qkv || !positions || !rope_cos || !rope_sin || !k_cache || !v_cache || !out) return BITNET_ERR_INVALID_ARGUMENT;
   if (B <= 0 || n_kv_heads <= 0 || n_heads <= 0 || n_heads % n_kv_heads != 0 || head_dim != ATT_D || max_len <= 0 ||
-      rope_len <= 0)
+      rope_len <= 0 || max_ctx < 0)
     return BITNET_ERR_INVALID_ARGUMENT;
-  if (!aligned(k_cache, 16) || !aligned(v_cache, 16) || !aligned(qkv, 2) || !aligned(out, 2))
+  if (max_ctx == 0) max_ctx = std::min(max_len, rope_len);
+  if (max_ctx > max_len || max_ctx > rope_len) return BITNET_ERR_INVALID_ARGUMENT;
+  if (!aligned(k_cache, 16) || !aligned(v_cache, 16) || !aligned(qkv, 4) || !aligned(out, 2))
     return BITNET_ERR_ALIGNMENT;
+  const size_t ws_need = bitnet_gqa_decode_workspace_bytes(B, n_heads, n_kv_heads, max_ctx);
+  if (ws_need > 0 && (workspace == nullptr || workspace_bytes < ws_need)) return BITNET_ERR_INVALID_ARGUMENT;
+  if (ws_need > 0 && !aligned(workspace, 16)) return BITNET_ERR_ALIGNMENT;
   AttnParams p;
   p.qkv = (const uint16_t*)qkv;
   p.n_heads = n_heads;
@@ -466,14 +485,28 @@ int bitnet_gqa_decode_attention(const void* qkv, int B, int n_heads, int n_kv_he
   p.k_cache = (uint16_t*)k_cache;
   p.v_cache = (uint16_t*)v_cache;
   p.max_len = max_len;
+  p.max_ctx = max_ctx;
+  p.nsplit = att_nsplit(max_ctx);
   p.scale = scale;
+  const size_t counters = ((size_t)B * n_kv_heads * sizeof(int) + 255) / 256 * 256;
+  p.ws_count = ws_need > 0 ? (int*)workspace : nullptr;
+  p.ws_part = ws_need > 0 ? (float*)((uint8_t*)workspace + counters) : nullptr;
   p.out = (uint16_t*)out;
-  const dim3 grid(B, n_kv_heads), block(ATT_THREADS);
+  const dim3 grid(B, n_kv_heads, p.nsplit), block(ATT_THREADS);
+  const size_t smem = att_smem_bytes(p.G);
   switch (p.G) {
-    case 1: return launch(gqa_decode_kernel<1>, grid, block, 0, stream, 1, p);
-    case 2: return launch(gqa_decode_kernel<2>, grid, block, 0, stream, 1, p);
-    case 4: return launch(gqa_decode_kernel<4>, grid, block, 0, stream, 1, p);
-    case 8: return launch(gqa_decode_kernel<8>, grid, block, 0, stream, 1, p);
+    case 1:
+      if (int e = ensure_smem(gqa_decode_kernel<1>, &g_smem_att[0])) return e;
+      return launch(gqa_decode_kernel<1>, grid, block, smem, stream, 1, p);
+    case 2:
+      if (int e = ensure_smem(gqa_decode_kernel<2>, &g_smem_att[1])) return e;
+      return launch(gqa_decode_kernel<2>, grid, block, smem, stream, 1, p);
+    case 4:
+      if (int e = ensure_smem(gqa_decode_kernel<4>, &g_smem_att[2])) return e;
+      return launch(gqa_decode_kernel<4>, grid, block, smem, stream, 1, p);
+    case 8:
+      if (int e = ensure_smem(gqa_decode_kernel<8>, &g_smem_att[3])) return e;
+      return launch(gqa_decode_kernel<8>, grid, block, smem, stream, 1, p);
     default: return BITNET_ERR_INVALID_ARGUMENT;
   }
 }

@@ -157,17 +157,27 @@ int bitnet_bitlinear_noalloc(const void* x, int M, int K, const void* gamma, flo
 /* ---- GQA decode attention with fused RoPE and KV append --------------------
  * Replaces nlp_create_qkv_heads_decode + rotary_embedding_llama +
  * paged_update_cache + scaled_dot_product_attention_decode +
- * nlp_concat_heads_decode (src/bitnet_tt/layers/attention.py:1040-1262).
- * qkv: bf16 [B, (n_heads + 2*n_kv_heads) * head_dim] (Q | K | V, already scaled).
+ * nlp_concat_heads_decode (src/bitnet_tt/layers/attention.py:1040-1262; the
+ * SDPA decode's chunked grid, attention.py:670-708, becomes a split of the
+ * context over CTAs of 256 keys with an in-kernel merge).
+ * qkv: bf16 [B, (n_heads + 2*n_kv_heads) * head_dim] (Q | K | V, already scaled),
+ * 4-byte aligned.
  * positions: int32 [B], the position of the token being decoded per sequence.
  * rope_cos / rope_sin: bf16 [rope_len, head_dim/2] (HF half-split convention).
  * k_cache / v_cache: bf16 [B, n_kv_heads, max_len, head_dim]; row `positions[b]`
  * is overwritten with the rotated K / V of this token.
+ * max_ctx: an upper bound on positions[b] + 1 for this call (0 = min(max_len,
+ * rope_len)); it sets the number of context splits, so a tight bound keeps the
+ * grid small.  A position at or above it is a device bounds error.
+ * workspace: bitnet_gqa_decode_workspace_bytes(B, n_heads, n_kv_heads, max_ctx)
+ * bytes, 16-byte aligned, ZEROED before its first use (the kernel leaves it
+ * zeroed); may be NULL when that size is 0 (max_ctx <= 256).
  * out: bf16 [B, n_heads * head_dim].  head_dim must be 128. */
+size_t bitnet_gqa_decode_workspace_bytes(int B, int n_heads, int n_kv_heads, int max_ctx);
 int bitnet_gqa_decode_attention(const void* qkv, int B, int n_heads, int n_kv_heads, int head_dim,
                                 const int32_t* positions, const void* rope_cos, const void* rope_sin,
-                                int rope_len, void* k_cache, void* v_cache, int max_len, float scale, void* out,
-                                bitnet_stream_t stream);
+                                int rope_len, void* k_cache, void* v_cache, int max_len, int max_ctx, float scale,
+                                void* workspace, size_t workspace_bytes, void* out, bitnet_stream_t stream);
 
 /* ---- lm_head / embedding table -------------------------------------------
  * The tied embedding / lm_head matrix (src/bitnet_tt/utils/weights.py:236-246)

@@ -32,7 +32,7 @@ def test_status_strings_and_sizes():
     from bitnet_tt import _lib
 
     lib = _lib.load()
-    assert lib.bitnet_abi_version() == 1
+    assert lib.bitnet_abi_version() == 2
     assert _lib.status_string(0) == "ok"
     assert "invalid argument" in _lib.status_string(-1)
     assert "unknown" in _lib.status_string(-99)
@@ -45,6 +45,12 @@ def test_status_strings_and_sizes():
     # per-CTA (max, idx) pairs for up to 160 CTAs, then the hidden states tiled (K x T bf16)
     assert _lib.argmax_workspace_bytes(32, 2560, 128256) == 160 * 32 * 8 + 2560 * 32 * 2
     assert lib.bitnet_packed_weight_bytes(0, 5) == 0
+    # attention: no workspace up to 256 keys; else 256-byte aligned counters,
+    # then per (sequence, KV head, split) 2G + 128G floats
+    assert _lib.gqa_decode_workspace_bytes(32, 20, 5, 256) == 0
+    assert _lib.gqa_decode_workspace_bytes(32, 20, 5, 257) == 768 + 32 * 5 * 2 * (8 + 512) * 4
+    assert _lib.gqa_decode_workspace_bytes(32, 20, 5, 4096) == 768 + 32 * 5 * 16 * (8 + 512) * 4
+    assert _lib.gqa_decode_workspace_bytes(32, 20, 3, 4096) == 0  # heads not a multiple of KV heads
 
 
 def test_option_validation_is_host_side():

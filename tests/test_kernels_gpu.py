@@ -67,7 +67,8 @@ def run_act_quant(x: torch.Tensor, gamma: torch.Tensor | None, eps: float, cuda)
     return q, f32(bufs.row_scale)[:m], bufs.row_sum.cpu().numpy()[:m], f32(normed)
 
 
-@pytest.mark.parametrize("m,k", [(1, 64), (3, 100), (8, 2560), (32, 2560), (32, 6912), (40, 320), (300, 128)])
+@pytest.mark.parametrize("m,k", [(1, 64), (3, 100), (8, 2560), (32, 2560), (32, 6912), (40, 320), (300, 128),
+                                 (2, 8192), (2, 8200)])
 @pytest.mark.parametrize("with_gamma", [True, False])
 def test_act_quant_bit_exact(cuda, m, k, with_gamma):
     x = rand_bf16((m, k), seed=m * 1000 + k)

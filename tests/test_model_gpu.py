@@ -41,22 +41,26 @@ def _device_model(cfg, sd, cuda):
 
 
 # ---------------------------------------------------------------------------
-def test_attention_kernel_rope_append_and_softmax(cuda):
+def _attention_case(cuda, b, nh, nkv, max_len, pos_list, max_ctx=0, seed=11):
     from bitnet_tt import _lib
     from bitnet_tt.utils.rope import half_split_tables
 
-    b, nh, nkv, d, max_len = 4, 20, 5, 128, 300
-    g = torch.Generator().manual_seed(11)
+    d = 128
+    g = torch.Generator().manual_seed(seed)
     qkv = torch.randn((b, (nh + 2 * nkv) * d), generator=g).to(torch.bfloat16)
     kc = torch.randn((b, nkv, max_len, d), generator=g).to(torch.bfloat16)
     vc = torch.randn((b, nkv, max_len, d), generator=g).to(torch.bfloat16)
-    pos = torch.tensor([0, 7, 130, 299], dtype=torch.int32)
+    pos = torch.tensor(pos_list, dtype=torch.int32)
     cos, sin = half_split_tables(d, max_len, 500000.0)
     out = torch.empty((b, nh * d), dtype=torch.bfloat16, device=cuda)
     kd, vd = kc.to(cuda), vc.to(cuda)
-    _lib.gqa_decode_attention(qkv.to(cuda), nh, nkv, d, pos.to(cuda), cos.to(cuda), sin.to(cuda), kd, vd, d ** -0.5, out)
+    ws = _lib.gqa_decode_workspace(b, nh, nkv, max_ctx or max_len, cuda)
+    _lib.gqa_decode_attention(qkv.to(cuda), nh, nkv, d, pos.to(cuda), cos.to(cuda), sin.to(cuda), kd, vd, d ** -0.5,
+                              out, max_ctx, ws)
     torch.cuda.synchronize()
     assert _lib.last_device_status()[0] == 0
+    if ws is not None:  # the kernel leaves its arrival counters at zero
+        assert int(ws[: b * nkv * 4].view(torch.int32).abs().sum()) == 0
 
     o = om.OracleBitNet.__new__(om.OracleBitNet)
     o.d, o.nq, o.nkv = d, nh, nkv
@@ -68,7 +72,51 @@ def test_attention_kernel_rope_append_and_softmax(cuda):
         p = int(pos[i])
         np.testing.assert_array_equal(kd[i, :, p].float().cpu().numpy(), cache[0][i, :, p].numpy())
         np.testing.assert_array_equal(vd[i, :, p].float().cpu().numpy(), cache[1][i, :, p].numpy())
+    # the rest of the cache is untouched
+    mask = torch.ones((b, max_len), dtype=torch.bool)
+    mask[torch.arange(b), pos.long()] = False
+    assert torch.equal(kd.cpu().permute(0, 2, 1, 3)[mask], kc.permute(0, 2, 1, 3)[mask])
     np.testing.assert_allclose(out.float().cpu().numpy(), ref.numpy(), rtol=2e-2, atol=2e-2)
+
+
+def test_attention_kernel_rope_append_and_softmax(cuda):
+    _attention_case(cuda, 4, 20, 5, 300, [0, 7, 130, 299], max_ctx=300)
+
+
+@pytest.mark.parametrize("nh,nkv", [(4, 4), (4, 2), (8, 2), (16, 2)])
+def test_attention_group_sizes(cuda, nh, nkv):
+    _attention_case(cuda, 3, nh, nkv, 200, [5, 16, 199], seed=nh * 10 + nkv)
+
+
+def test_attention_split_context_ragged(cuda):
+    # ragged contexts across several 256-key splits (config-4 style lengths)
+    _attention_case(cuda, 6, 20, 5, 4096, [0, 255, 256, 1000, 2047, 4095], seed=3)
+
+
+def test_attention_split_repeated_calls(cuda):
+    # the workspace counters must return to zero so that later calls merge correctly
+    for rep in range(3):
+        _attention_case(cuda, 2, 8, 2, 1024, [600 + rep, 1023 - rep], seed=20 + rep)
+
+
+def test_attention_position_beyond_max_ctx_is_a_device_error(cuda):
+    from bitnet_tt import _lib
+    from bitnet_tt.utils.rope import half_split_tables
+
+    b, nh, nkv, d, max_len = 2, 4, 2, 128, 512
+    qkv = torch.zeros((b, (nh + 2 * nkv) * d), dtype=torch.bfloat16, device=cuda)
+    kd = torch.zeros((b, nkv, max_len, d), dtype=torch.bfloat16, device=cuda)
+    vd = torch.zeros_like(kd)
+    cos, sin = half_split_tables(d, max_len, 500000.0)
+    out = torch.empty((b, nh * d), dtype=torch.bfloat16, device=cuda)
+    pos = torch.tensor([3, 300], dtype=torch.int32, device=cuda)
+    _lib.gqa_decode_attention(qkv, nh, nkv, d, pos, cos.to(cuda), sin.to(cuda), kd, vd, 1.0, out, 256, None)
+    torch.cuda.synchronize()
+    code, site = _lib.last_device_status()
+    assert code == -1 and site == 300  # a kernel bounds check reads back as BITNET_ERR_INVALID_ARGUMENT
+    # a split context needs its workspace
+    with pytest.raises(RuntimeError):
+        _lib.gqa_decode_attention(qkv, nh, nkv, d, pos, cos.to(cuda), sin.to(cuda), kd, vd, 1.0, out, 512, None)
 
 
 def test_lm_head_argmax_and_embedding(cuda):
