@@ -65,6 +65,8 @@ def parse() -> argparse.Namespace:
     p.add_argument("--e2e-steps", type=int, default=256)
     p.add_argument("--cpu-baseline-steps", type=int, default=2, help="0 disables the CPU baseline")
     p.add_argument("--ref-budget-s", type=float, default=60.0, help="timed CPU work of --impl reference")
+    p.add_argument("--decode-path", choices=["per-op", "persistent"], default="per-op",
+                   help="per-op: 9 launches per layer; persistent: every layer in one launch")
     return p.parse_args()
 
 
@@ -306,6 +308,10 @@ def kernel_rooflines(gen, args, hbm_peak: float) -> dict:
                                                               st.attn, st.max_ctx, st.attn_ws)
                                 for L, c in zip(m.layers, st.caches)], nl,
           kv_bytes + 2 * b * qkv_n + 2 * b * h, nl)
+    if gen.persistent:
+        # every layer in one persistent launch: all packed weights + the KV rows read + activations
+        layer_w = wbytes(qkv_n, h) + wbytes(h, h) + wbytes(2 * f, h) + wbytes(h, f)
+        entry("decode_layers", lambda: st.plan.run(), 1, nl * (layer_w + kv_bytes + 2 * b * (qkv_n + 3 * h + 2 * f)), 1)
     ws = st.argmax_ws
     ids = torch.empty_like(st.ids)
     entry("lm_head", lambda: m.lm_head_argmax(st.normed, ws, ids), 1, 2 * v * h + 2 * b * h, 1)  # 3 launches
@@ -332,7 +338,8 @@ def run_b200(args) -> None:
     t_build = time.perf_counter() - t_build
 
     b = args.batch
-    gen = Batch32Generator(model, batch_size=b, max_seq_len=args.max_seq_len)
+    gen = Batch32Generator(model, batch_size=b, max_seq_len=args.max_seq_len,
+                           persistent=args.decode_path == "persistent")
     gen.set_context_limit(args.prompt_len + args.new_tokens)  # positions cycle within it
     rng = np.random.default_rng(args.seed * 1000 + rank)
     prompts = rng.integers(0, cfg.vocab_size, size=(b, args.prompt_len))
@@ -416,7 +423,7 @@ def run_b200(args) -> None:
         roof = {"kernel": dominant, "bound": "hbm", "achieved": round(d["achieved_gbs"], 1),
                 "peak": hbm_peak, "unit": "GB/s", "frac": round(d["frac"], 4), "traffic": d["traffic"],
                 "peak_kind": peak_kind}
-    launches = args.steps * gen_launches(cfg)
+    launches = args.steps * gen.launches_per_step
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
@@ -426,6 +433,7 @@ def run_b200(args) -> None:
                                "128 new tokens, bf16 KV cache 2048, CUDA graph",
                    "batch_per_gpu": b, "global_batch": b * world, "prompt_len": args.prompt_len,
                    "new_tokens": args.new_tokens, "layers": args.layers, "parallelism": f"dp{world} (batch split)",
+                   "decode_path": args.decode_path,
                    "l2": "inputs larger than L2 (1.26 GB weights streamed per step)",
                    "model_build_s": round(t_build, 1)},
         "e2e": {"value": round(e2e_value, 1), "unit": "tok/s", "h2d_bytes_per_step": 4 * b,
@@ -439,12 +447,6 @@ def run_b200(args) -> None:
         "device_status": status[0],
     }
     print(json.dumps(line), flush=True)
-
-
-def gen_launches(cfg) -> int:
-    """Kernels of one decode step: embedding gather; per layer 4 act-quant, 4
-    BitLinear, 1 attention; final norm, hidden-state tiling, lm_head, argmax reduce."""
-    return 1 + 9 * cfg.num_layers + 4
 
 
 def main() -> None:

@@ -49,6 +49,56 @@ class Segments(ctypes.Structure):
         return s
 
 
+class DecodeLayer(ctypes.Structure):
+    """bitnet_decode_layer_t."""
+
+    _fields_ = [
+        ("w_qkv", ctypes.c_void_p),
+        ("w_o", ctypes.c_void_p),
+        ("w_gate_up", ctypes.c_void_p),
+        ("w_down", ctypes.c_void_p),
+        ("seg_qkv", Segments),
+        ("seg_o", Segments),
+        ("seg_gate_up", Segments),
+        ("seg_down", Segments),
+        ("input_layernorm", ctypes.c_void_p),
+        ("attn_sub_norm", ctypes.c_void_p),
+        ("post_attention_layernorm", ctypes.c_void_p),
+        ("ffn_sub_norm", ctypes.c_void_p),
+        ("k_cache", ctypes.c_void_p),
+        ("v_cache", ctypes.c_void_p),
+    ]
+
+
+class DecodeDesc(ctypes.Structure):
+    """bitnet_decode_desc_t."""
+
+    _fields_ = [
+        ("num_layers", ctypes.c_int),
+        ("batch", ctypes.c_int),
+        ("hidden", ctypes.c_int),
+        ("intermediate", ctypes.c_int),
+        ("n_heads", ctypes.c_int),
+        ("n_kv_heads", ctypes.c_int),
+        ("head_dim", ctypes.c_int),
+        ("eps", ctypes.c_float),
+        ("layers", ctypes.POINTER(DecodeLayer)),
+        ("hidden_state", ctypes.c_void_p),
+        ("qkv", ctypes.c_void_p),
+        ("attn", ctypes.c_void_p),
+        ("mid", ctypes.c_void_p),
+        ("positions", ctypes.c_void_p),
+        ("rope_cos", ctypes.c_void_p),
+        ("rope_sin", ctypes.c_void_p),
+        ("rope_len", ctypes.c_int),
+        ("max_len", ctypes.c_int),
+        ("max_ctx", ctypes.c_int),
+        ("attn_workspace", ctypes.c_void_p),
+        ("attn_workspace_bytes", ctypes.c_size_t),
+        ("splits", ctypes.c_int * 4),
+    ]
+
+
 # name -> (restype, argtypes)
 _SIGNATURES = {
     "bitnet_abi_version": (_c_int, []),
@@ -89,6 +139,9 @@ _SIGNATURES = {
         [_c_void_p, _c_int, _c_int, _c_int, _c_int, _c_void_p, _c_void_p, _c_void_p, _c_int, _c_void_p, _c_void_p,
          _c_int, _c_int, _c_float, _c_void_p, _c_size_t, _c_void_p, _c_void_p],
     ),
+    "bitnet_decode_plan_create": (_c_int, [ctypes.POINTER(DecodeDesc), ctypes.POINTER(_c_void_p)]),
+    "bitnet_decode_plan_run": (_c_int, [_c_void_p, _c_void_p]),
+    "bitnet_decode_plan_destroy": (_c_int, [_c_void_p]),
     "bitnet_lm_head_bytes": (_c_size_t, [_c_int, _c_int]),
     "bitnet_pack_lm_head": (_c_int, [_c_void_p, _c_int, _c_int, _c_void_p, _c_void_p]),
     "bitnet_embed_gather": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_int, _c_int, _c_void_p, _c_void_p]),
@@ -294,3 +347,61 @@ def lm_head_argmax(h: torch.Tensor, w_tiled: torch.Tensor, v: int, workspace: to
     check(load().bitnet_lm_head_argmax(ptr(h), b, k, ptr(w_tiled), v, ptr(workspace), ptr(out_ids),
                                        ptr(logits_out), ptr(advance_positions), stream_handle()),
           "bitnet_lm_head_argmax")
+
+
+class DecodePlan:
+    """All transformer layers of a decode step in one persistent launch
+    (bitnet_decode_plan_*).  Holds references to every tensor it points at."""
+
+    def __init__(self, model, hidden: torch.Tensor, qkv: torch.Tensor, attn: torch.Tensor, mid: torch.Tensor,
+                 positions: torch.Tensor, rope_cos: torch.Tensor, rope_sin: torch.Tensor, caches,
+                 max_ctx: int = 0, attn_workspace: torch.Tensor | None = None,
+                 splits: tuple[int, int, int, int] | None = None) -> None:
+        cfg = model.config
+        n = cfg.num_layers
+        layers = (DecodeLayer * n)()
+        keep = [hidden, qkv, attn, mid, positions, rope_cos, rope_sin, attn_workspace]
+        for i, (blk, cache) in enumerate(zip(model.layers, caches)):
+            at, mlp = blk.self_attn, blk.mlp
+            L = layers[i]
+            L.w_qkv, L.w_o = ptr(at.qkv_proj.weight), ptr(at.o_proj.weight)
+            L.w_gate_up, L.w_down = ptr(mlp.gate_up_proj.weight), ptr(mlp.down_proj.weight)
+            L.seg_qkv, L.seg_o = at.qkv_proj.segments(), at.o_proj.segments()
+            L.seg_gate_up, L.seg_down = mlp.gate_up_proj.segments(), mlp.down_proj.segments()
+            L.input_layernorm = ptr(blk.input_layernorm.weight)
+            L.attn_sub_norm = ptr(at.attn_sub_norm.weight)
+            L.post_attention_layernorm = ptr(blk.post_attention_layernorm.weight)
+            L.ffn_sub_norm = ptr(mlp.ffn_sub_norm.weight)
+            L.k_cache, L.v_cache = ptr(cache.key_cache), ptr(cache.value_cache)
+            keep += [at.qkv_proj.weight, at.o_proj.weight, mlp.gate_up_proj.weight, mlp.down_proj.weight,
+                     cache.key_cache, cache.value_cache]
+        d = DecodeDesc()
+        d.num_layers, d.batch, d.hidden = n, hidden.shape[0], cfg.hidden_size
+        d.intermediate, d.n_heads, d.n_kv_heads = cfg.intermediate_size, cfg.num_attention_heads, cfg.num_key_value_heads
+        d.head_dim, d.eps = cfg.head_dim, cfg.rms_norm_eps
+        d.layers = layers
+        d.hidden_state, d.qkv, d.attn, d.mid = ptr(hidden), ptr(qkv), ptr(attn), ptr(mid)
+        d.positions, d.rope_cos, d.rope_sin = ptr(positions), ptr(rope_cos), ptr(rope_sin)
+        d.rope_len, d.max_len, d.max_ctx = rope_cos.shape[0], caches[0].key_cache.shape[2], int(max_ctx)
+        d.attn_workspace = ptr(attn_workspace)
+        d.attn_workspace_bytes = attn_workspace.numel() if attn_workspace is not None else 0
+        for i, v in enumerate(splits or (0, 0, 0, 0)):
+            d.splits[i] = int(v)
+        h = _c_void_p()
+        check(load().bitnet_decode_plan_create(ctypes.byref(d), ctypes.byref(h)), "bitnet_decode_plan_create")
+        self._h = h
+        self._keep = keep
+
+    def run(self) -> None:
+        check(load().bitnet_decode_plan_run(self._h, stream_handle()), "bitnet_decode_plan_run")
+
+    def close(self) -> None:
+        if getattr(self, "_h", None) is not None and self._h.value:
+            load().bitnet_decode_plan_destroy(self._h)
+            self._h = _c_void_p()
+
+    def __del__(self) -> None:
+        try:
+            self.close()
+        except Exception:
+            pass

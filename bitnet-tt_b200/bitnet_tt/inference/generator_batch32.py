@@ -86,6 +86,7 @@ class DecodeState:
         cos, sin = half_split_tables(cfg.head_dim, max_seq_len, cfg.rope_theta)
         self.rope_cos, self.rope_sin = cos.to(dev), sin.to(dev)
         self.logits: torch.Tensor | None = None
+        self.plan: _lib.DecodePlan | None = None  # persistent all-layer launch (built outside capture)
 
     def kv_bytes(self) -> int:
         return sum(c.key_cache.numel() * 2 * 2 for c in self.caches)
@@ -93,7 +94,7 @@ class DecodeState:
 
 class Batch32Generator:
     def __init__(self, model, tokenizer: Any = None, enable_trace: bool = True, batch_size: int = PADDED_BATCH,
-                 max_seq_len: int = 2048, keep_logits: bool = False) -> None:
+                 max_seq_len: int = 2048, keep_logits: bool = False, persistent: bool | None = None) -> None:
         self.model = model
         self.device = model.device
         self.config = model.config
@@ -104,7 +105,9 @@ class Batch32Generator:
         self.keep_logits = keep_logits
         self.state: DecodeState | None = None
         self._graph: torch.cuda.CUDAGraph | None = None
-        self.launches_per_step = 9 * self.config.num_layers + 5
+        # persistent=True: every layer in one launch (batch <= 32); default: 9 launches per layer
+        self.persistent = bool(persistent) and batch_size <= PADDED_BATCH
+        self.launches_per_step = 6 if self.persistent else 9 * self.config.num_layers + 5
         self.last_stats = GenerationStats()
         self.context_limit = max_seq_len
 
@@ -119,6 +122,7 @@ class Batch32Generator:
             if self.state is not None:
                 st = self.state
                 st.max_ctx = n
+                st.plan = None
                 st.attn_ws = _lib.gqa_decode_workspace(self.batch_size, self.config.num_attention_heads,
                                                        self.config.num_key_value_heads, n, self.device)
 
@@ -137,7 +141,12 @@ class Batch32Generator:
         m, cfg = self.model, self.config
         b, eps = st.batch, cfg.rms_norm_eps
         m.embed_tokens.gather_into(st.ids, st.hidden)
-        for layer, cache in zip(m.layers, st.caches):
+        if self.persistent:
+            if st.plan is None:
+                st.plan = _lib.DecodePlan(m, st.hidden, st.qkv, st.attn, st.mid, st.positions, st.rope_cos,
+                                          st.rope_sin, st.caches, st.max_ctx, st.attn_ws)
+            st.plan.run()
+        for layer, cache in zip(m.layers, st.caches) if not self.persistent else ():
             attn = layer.self_attn
             _lib.act_quant(st.hidden, layer.input_layernorm.weight, eps, st.act_h)
             attn.qkv_proj.forward_into(st.act_h, b, st.qkv)

@@ -110,11 +110,12 @@ act_quant_kernel(const uint16_t* __restrict__ x, int M, int K, int ldx, const ui
 }
 
 // Fast path: K % 8 == 0, 16-byte aligned rows (ldx % 8 == 0) and gamma, and
-// K <= 8 * 256 * AQ_MAXC.  Each thread keeps up to AQ_MAXC 8-element chunks in
-// registers (16-byte loads; gamma is read before griddepcontrol.wait, since it
-// does not come from the previous kernel), and the three reductions use one
-// barrier each.  Same results as act_quant_kernel (the fp64 sum of squares is
-// exact in any order; max and the integer sum are order-free).
+// K <= 8 * 256 * AQ_MAXC.  A row runs on 256 threads; each keeps up to
+// AQ_MAXC 8-element chunks in registers (16-byte loads), and the three
+// reductions use one barrier each (separate scratch words per reduction, so a
+// reduction's scratch is never rewritten before every thread has read it).
+// Same results as act_quant_kernel (the fp64 sum of squares is exact in any
+// order; max and the integer sum are order-free).
 constexpr int AQ_THREADS = 256;
 constexpr int AQ_MAXC = 4;
 
@@ -127,17 +128,135 @@ __device__ __forceinline__ void aq_unpack8(const uint4 v, float* f) {
   }
 }
 
-template <typename T, typename Op>
-__device__ __forceinline__ T block_allreduce_once(T v, T* scratch, Op op) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+// Barrier over the row's 256 threads: __syncthreads (BAR == 0) or named barrier BAR.
+template <int BAR>
+__device__ __forceinline__ void aq_sync() {
+  if (BAR == 0)
+    __syncthreads();
+  else
+    named_bar_sync(BAR, AQ_THREADS);
+}
+
+struct AqScratch {
+  double* d;  // [8]
+  float* f;   // [8]
+  int* i;     // [8]
+};
+
+template <int BAR, typename T, typename Op>
+__device__ __forceinline__ T aq_allreduce(T v, T* scratch, Op op, int t) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = op(v, __shfl_xor_sync(0xffffffffu, v, o));
-  if (lane == 0) scratch[warp] = v;
-  __syncthreads();
+  if ((t & 31) == 0) scratch[t >> 5] = v;
+  aq_sync<BAR>();
   T r = scratch[0];
 #pragma unroll
   for (int i = 1; i < AQ_THREADS / 32; ++i) r = op(r, scratch[i]);
   return r;
+}
+
+// gamma chunks of thread t, kept packed (bf16 x 8 per register quad); gamma
+// does not come from the previous kernel, so the standalone kernel loads it
+// before griddepcontrol.wait
+__device__ __forceinline__ void aq_load_gamma(uint4 (&gr)[AQ_MAXC], const uint16_t* gamma, int K, int t) {
+#pragma unroll
+  for (int c = 0; c < AQ_MAXC; ++c) {
+    const int ch = t + c * AQ_THREADS;
+    gr[c] = (gamma != nullptr && ch < (K >> 3)) ? reinterpret_cast<const uint4*>(gamma)[ch] : make_uint4(0, 0, 0, 0);
+  }
+}
+
+__device__ __forceinline__ uint4 aq_pack8(const float* f) {
+  uint4 o;
+  o.x = (uint32_t)f32_to_bf16_bits(f[0]) | ((uint32_t)f32_to_bf16_bits(f[1]) << 16);
+  o.y = (uint32_t)f32_to_bf16_bits(f[2]) | ((uint32_t)f32_to_bf16_bits(f[3]) << 16);
+  o.z = (uint32_t)f32_to_bf16_bits(f[4]) | ((uint32_t)f32_to_bf16_bits(f[5]) << 16);
+  o.w = (uint32_t)f32_to_bf16_bits(f[6]) | ((uint32_t)f32_to_bf16_bits(f[7]) << 16);
+  return o;
+}
+
+// Row m (padded rows m >= M produce zero codes, scale 1, sum 0) on threads
+// t = 0..255.  The row stays in registers as packed bf16: the input is bf16 and
+// every normalised value is rounded to bf16, so repacking loses nothing.
+template <int BAR>
+__device__ void aq_row_vec(const uint16_t* __restrict__ x, int M, int K, int ldx, bool has_gamma,
+                           const uint4 (&gr)[AQ_MAXC], float eps, int8_t* __restrict__ q,
+                           float* __restrict__ row_scale, int32_t* __restrict__ row_sum,
+                           uint16_t* __restrict__ normed_out, int T, int Kp, int m, const AqScratch& sc, int t) {
+  const bool valid = m < M;
+  const int KC8 = K >> 3;  // chunks of 8
+  uint4 xr[AQ_MAXC];
+#pragma unroll
+  for (int c = 0; c < AQ_MAXC; ++c) {
+    const int ch = t + c * AQ_THREADS;
+    xr[c] = (valid && ch < KC8) ? reinterpret_cast<const uint4*>(x + (size_t)m * ldx)[ch] : make_uint4(0, 0, 0, 0);
+  }
+  if (has_gamma) {
+    double ss = 0.0;
+#pragma unroll
+    for (int c = 0; c < AQ_MAXC; ++c) {
+      float f[8];
+      aq_unpack8(xr[c], f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss = fma((double)f[e], (double)f[e], ss);
+    }
+    ss = aq_allreduce<BAR>(ss, sc.d, OpAddD(), t);
+    const float var = __double2float_rn(__ddiv_rn(ss, (double)K));
+    const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+#pragma unroll
+    for (int c = 0; c < AQ_MAXC; ++c) {
+      float f[8], g[8];
+      aq_unpack8(xr[c], f);
+      aq_unpack8(gr[c], g);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) f[e] = round_bf16(__fmul_rn(g[e], round_bf16(__fmul_rn(f[e], r))));
+      xr[c] = aq_pack8(f);
+    }
+  }
+  if (normed_out != nullptr && valid) {
+#pragma unroll
+    for (int c = 0; c < AQ_MAXC; ++c) {
+      const int ch = t + c * AQ_THREADS;
+      if (ch < KC8) reinterpret_cast<uint4*>(normed_out + (size_t)m * K)[ch] = xr[c];
+    }
+  }
+  if (q == nullptr) return;
+  float amax = 0.f;
+#pragma unroll
+  for (int c = 0; c < AQ_MAXC; ++c) {
+    float f[8];
+    aq_unpack8(xr[c], f);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(f[e]));
+  }
+  amax = fmaxf(aq_allreduce<BAR>(amax, sc.f, OpMaxF(), t), 1e-5f);
+  const float s = __fdiv_rn(127.0f, amax);
+  int qsum = 0;
+#pragma unroll
+  for (int c = 0; c < AQ_MAXC; ++c) {
+    const int ch = t + c * AQ_THREADS;
+    if (ch * 8 < Kp) {  // chunks past K (up to Kp) are written as zeros
+      float f[8];
+      aq_unpack8(xr[c], f);
+      uint32_t lo = 0, hi = 0;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        int qi = 0;
+        if (valid && ch < KC8) qi = max(-128, min(127, __float2int_rn(__fmul_rn(f[e], s))));
+        qsum += qi;
+        if (e < 4)
+          lo |= ((uint32_t)(qi & 0xFF)) << (8 * e);
+        else
+          hi |= ((uint32_t)(qi & 0xFF)) << (8 * (e - 4));
+      }
+      *reinterpret_cast<uint2*>(q + alayout_offset(m, ch * 8, T, Kp)) = make_uint2(lo, hi);
+    }
+  }
+  qsum = aq_allreduce<BAR>(qsum, sc.i, OpAddI(), t);
+  if (t == 0) {
+    row_scale[m] = valid ? s : 1.0f;
+    row_sum[m] = qsum;
+  }
 }
 
 __global__ void __launch_bounds__(AQ_THREADS)
@@ -148,85 +267,12 @@ act_quant_vec_kernel(const uint16_t* __restrict__ x, int M, int K, int ldx, cons
   __shared__ float red_f[AQ_THREADS / 32];
   __shared__ int red_i[AQ_THREADS / 32];
   pdl_trigger();
-  const int m = blockIdx.x, tid = threadIdx.x;
-  const bool valid = m < M;
-  const int KC8 = K >> 3;  // chunks of 8
-  float gm[AQ_MAXC][8];
-#pragma unroll
-  for (int c = 0; c < AQ_MAXC; ++c) {
-    const int ch = tid + c * AQ_THREADS;
-    if (gamma != nullptr && ch < KC8) aq_unpack8(reinterpret_cast<const uint4*>(gamma)[ch], gm[c]);
-  }
+  uint4 gr[AQ_MAXC];
+  aq_load_gamma(gr, gamma, K, threadIdx.x);
   pdl_wait();
-  float v[AQ_MAXC][8];
-  double ss = 0.0;
-#pragma unroll
-  for (int c = 0; c < AQ_MAXC; ++c) {
-    const int ch = tid + c * AQ_THREADS;
-    if (valid && ch < KC8) {
-      aq_unpack8(reinterpret_cast<const uint4*>(x + (size_t)m * ldx)[ch], v[c]);
-    } else {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) v[c][e] = 0.f;
-    }
-#pragma unroll
-    for (int e = 0; e < 8; ++e) ss = fma((double)v[c][e], (double)v[c][e], ss);
-  }
-  if (gamma != nullptr) {
-    ss = block_allreduce_once(ss, red_d, OpAddD());
-    const float var = __double2float_rn(__ddiv_rn(ss, (double)K));
-    const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
-#pragma unroll
-    for (int c = 0; c < AQ_MAXC; ++c)
-#pragma unroll
-      for (int e = 0; e < 8; ++e) v[c][e] = round_bf16(__fmul_rn(gm[c][e], round_bf16(__fmul_rn(v[c][e], r))));
-  }
-  if (normed_out != nullptr && valid) {
-#pragma unroll
-    for (int c = 0; c < AQ_MAXC; ++c) {
-      const int ch = tid + c * AQ_THREADS;
-      if (ch < KC8) {
-        uint4 o;
-        o.x = (uint32_t)f32_to_bf16_bits(v[c][0]) | ((uint32_t)f32_to_bf16_bits(v[c][1]) << 16);
-        o.y = (uint32_t)f32_to_bf16_bits(v[c][2]) | ((uint32_t)f32_to_bf16_bits(v[c][3]) << 16);
-        o.z = (uint32_t)f32_to_bf16_bits(v[c][4]) | ((uint32_t)f32_to_bf16_bits(v[c][5]) << 16);
-        o.w = (uint32_t)f32_to_bf16_bits(v[c][6]) | ((uint32_t)f32_to_bf16_bits(v[c][7]) << 16);
-        reinterpret_cast<uint4*>(normed_out + (size_t)m * K)[ch] = o;
-      }
-    }
-  }
-  if (q == nullptr) return;
-  float amax = 0.f;
-#pragma unroll
-  for (int c = 0; c < AQ_MAXC; ++c)
-#pragma unroll
-    for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(v[c][e]));
-  amax = fmaxf(block_allreduce_once(amax, red_f, OpMaxF()), 1e-5f);
-  const float s = __fdiv_rn(127.0f, amax);
-  int qsum = 0;
-#pragma unroll
-  for (int c = 0; c < AQ_MAXC; ++c) {
-    const int ch = tid + c * AQ_THREADS;
-    if (ch * 8 < Kp) {  // chunks past K (up to Kp) are written as zeros
-      uint32_t lo = 0, hi = 0;
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        int qi = 0;
-        if (valid && ch < KC8) qi = max(-128, min(127, __float2int_rn(__fmul_rn(v[c][e], s))));
-        qsum += qi;
-        if (e < 4)
-          lo |= ((uint32_t)(qi & 0xFF)) << (8 * e);
-        else
-          hi |= ((uint32_t)(qi & 0xFF)) << (8 * (e - 4));
-      }
-      *reinterpret_cast<uint2*>(q + alayout_offset(m, ch * 8, T, Kp)) = make_uint2(lo, hi);
-    }
-  }
-  qsum = block_allreduce_once(qsum, red_i, OpAddI());
-  if (tid == 0) {
-    row_scale[m] = valid ? s : 1.0f;
-    row_sum[m] = qsum;
-  }
+  const AqScratch sc{red_d, red_f, red_i};
+  aq_row_vec<0>(x, M, K, ldx, gamma != nullptr, gr, eps, q, row_scale, row_sum, normed_out, T, Kp, blockIdx.x, sc,
+                threadIdx.x);
 }
 
 }  // namespace bitnet

@@ -1,41 +1,48 @@
 // GQA decode attention with fused rotary embedding and KV-cache append.
 //
-// Grid (B, n_kv_heads, S): CTA (b, g, s) serves the G = n_heads / n_kv_heads
-// query heads that share KV head g (HF repeat_kv grouping: query head h uses KV
-// head h / G) over keys [s * ATT_SPLIT_KEYS, (s + 1) * ATT_SPLIT_KEYS) of
-// sequence b.  Only the ceil(L / ATT_SPLIT_KEYS) CTAs whose range holds keys do
-// work (L = positions[b] + 1); the rest return at once.
+// Work unit (b, g, s): the G = n_heads / n_kv_heads query heads that share KV
+// head g (HF repeat_kv grouping: query head h uses KV head h / G) of sequence b,
+// over keys [s * ATT_SPLIT_KEYS, (s + 1) * ATT_SPLIT_KEYS).  Only the
+// ceil(L / ATT_SPLIT_KEYS) units whose range holds keys do work
+// (L = positions[b] + 1).  A unit runs on 4 warps:
 //   1. RoPE (HF half-split convention, bf16 op-by-op like transformers'
 //      apply_rotary_pos_emb on bf16 tensors):
 //        out[i]    = bf16(bf16(x[i] * cos_i)    + bf16(-x[i+64] * sin_i))
 //        out[i+64] = bf16(bf16(x[i+64] * cos_i) + bf16( x[i]    * sin_i))
-//      on the G query heads and the new key; the CTA whose range holds the new
-//      position writes the rotated key and the value to row positions[b].
-//   2. Each warp streams 16-key tiles of K and V (4 KB each, rows contiguous in
-//      the cache) with bulk copies into a double buffer of its own and keeps an
-//      online softmax: scores q . k_t * scale in fp32 (lane = key x half of the
-//      head dimension), running max / sum, and the weighted sum of v_t (lane =
-//      4 dimensions).  The tile holding the new position takes the rotated key
-//      and the value from shared memory, not from the cache row being written.
-//   3. The warps' states merge in shared memory.  With one active CTA the
-//      result is normalised and written; otherwise each CTA writes its
-//      (max, sum, unnormalised accumulator) to the workspace and the last CTA
-//      of (b, g) to arrive (a counter in the workspace, reset by that CTA) merges
-//      the parts.
+//      on the G query heads and the new key; the unit whose range holds the
+//      new position writes the rotated key and the value to row positions[b].
+//   2. Warp w takes the 16-key tiles w, w + 4, ... of the range: K and V rows
+//      (4 KB each, contiguous in the cache) arrive by bulk copy into a double
+//      buffer of the warp's own, the first two issued before the RoPE so that
+//      their latency overlaps it; an online softmax runs across the tiles.  Scores q . k_t * scale in fp32
+//      (lane = key x half of the head dimension, 16-byte chunks visited in a
+//      key-rotated order so a shared-memory phase touches 8 bank groups; the
+//      queries are kept as fp32 in a padded layout for the same reason), the
+//      tile's softmax state (max, sum), and P.V (lane = 4 dimensions, the
+//      probabilities broadcast from shared memory).  The tile holding the new
+//      position takes the rotated key and the value from shared memory, not
+//      from the cache row being written.
+//   3. The warps' states merge in shared memory.  With one active unit per
+//      (b, g) the result is normalised and written; otherwise each unit writes
+//      (max, sum, unnormalised accumulator) to the workspace and the last unit
+//      of (b, g) to finish (a counter in the workspace, reset by that unit)
+//      merges the parts.
 #pragma once
 #include "common.cuh"
 
 namespace bitnet {
 
-constexpr int ATT_THREADS = 128;
+constexpr int ATT_THREADS = 128;                     // one unit = 4 warps
 constexpr int ATT_WARPS = ATT_THREADS / 32;
 constexpr int ATT_D = 128;
 constexpr int ATT_MAX_G = 8;
-constexpr int ATT_TILE = 16;                            // keys per warp tile
-constexpr int ATT_NBUF = 2;                             // tiles in flight per warp
-constexpr int ATT_TILE_BYTES = ATT_TILE * ATT_D * 2;    // K (or V) of one tile
-constexpr int ATT_SPLIT_KEYS = 256;                     // keys per CTA
-constexpr int ATT_TILES_BYTES = ATT_WARPS * ATT_NBUF * 2 * ATT_TILE_BYTES;
+constexpr int ATT_TILE = 16;                         // keys per tile
+constexpr int ATT_TILES_PER_WARP = 4;
+constexpr int ATT_NBUF = 2;                          // tiles in flight per warp
+constexpr int ATT_TILE_BYTES = ATT_TILE * ATT_D * 2; // K (or V) of one tile
+constexpr int ATT_SPLIT_KEYS = ATT_WARPS * ATT_TILE * ATT_TILES_PER_WARP;  // keys per unit
+constexpr int ATT_TILES_BYTES = ATT_WARPS * ATT_NBUF * 2 * ATT_TILE_BYTES;  // 64 KB
+constexpr int ATT_QROW = 136;                        // bf16 per query row in shared memory (padded)
 
 struct AttnParams {
   const uint16_t* qkv;
@@ -54,74 +61,143 @@ struct AttnParams {
 };
 
 __host__ __device__ __forceinline__ int att_part_floats(int G) { return 2 * G + G * ATT_D; }
-__host__ __device__ __forceinline__ size_t att_smem_bytes(int G) {
-  return (size_t)ATT_TILES_BYTES + (size_t)G * ATT_D * 2 + 2 * ATT_D * 2 + ATT_WARPS * ATT_NBUF * 8;
+
+// Shared memory of one unit besides its tiles: rotated queries bf16
+// [G][ATT_QROW] | new key, new value (bf16) | mbarriers [warp][buffer].
+__host__ __device__ __forceinline__ size_t att_small_bytes(int G) {
+  return ((size_t)G * ATT_QROW * 2 + 2 * ATT_D * 2 + ATT_WARPS * ATT_NBUF * 8 + 127) / 128 * 128;
+}
+__host__ __device__ __forceinline__ size_t att_smem_bytes(int G) { return ATT_TILES_BYTES + att_small_bytes(G); }
+
+struct AttnSmem {
+  uint8_t* tiles;  // ATT_TILES_BYTES, 128-byte aligned
+  uint16_t* qb;
+  uint16_t* knew;
+  uint16_t* vnew;
+  uint64_t* bars;  // [warp][buffer], count 32 (one cp.async arrival per lane)
+  int* flag;       // one int: abort / "this unit merges"
+};
+
+__device__ __forceinline__ AttnSmem att_carve(uint8_t* tiles, uint8_t* small, int G, int* flag) {
+  AttnSmem s;
+  s.tiles = tiles;
+  s.qb = reinterpret_cast<uint16_t*>(small);
+  s.knew = s.qb + G * ATT_QROW;
+  s.vnew = s.knew + ATT_D;
+  s.bars = reinterpret_cast<uint64_t*>(s.vnew + ATT_D);
+  s.flag = flag;
+  return s;
+}
+// The barriers of a unit's tile buffers: one arrival per lane of the warp.
+constexpr int ATT_BAR_COUNT = 32;
+
+// Barrier over the unit's 128 threads (barrier 0 when the unit is the whole CTA).
+__device__ __forceinline__ void att_sync(int bar) { named_bar_sync(bar, ATT_THREADS); }
+
+// K / V tile layout in shared memory: row r (a key) is 256 bytes; its 16-byte
+// chunk c (8 dimensions) sits at chunk position c ^ (r & 7), so the 8 rows an
+// ldmatrix reads at one chunk fall in 8 different bank groups.
+__device__ __forceinline__ uint32_t att_swz(int r, int c) { return (uint32_t)(r * 256 + ((c ^ (r & 7)) << 4)); }
+
+__device__ __forceinline__ void cp_async16_zfill(uint32_t dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+// D = A (16x16 bf16, row) x B (16x8 bf16, col) + D, fp32 accumulate.  A rows
+// 8..15 are zero here (at most 8 query heads), so only a0 / a2 are passed.
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void mma_bf16_16816_full(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                                    uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  return (uint32_t)f32_to_bf16_bits(lo) | ((uint32_t)f32_to_bf16_bits(hi) << 16);
 }
 
-__device__ __forceinline__ void bf16x8_to_f32(const uint4 v, float* f) {
-  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    f[2 * e] = __uint_as_float(w[e] << 16);
-    f[2 * e + 1] = __uint_as_float(w[e] & 0xFFFF0000u);
-  }
-}
-
+// One unit on threads t = 0..127 of the caller, synchronised by barrier `bar`.
+// Warp w takes the tiles w, w + 4, w + 8, w + 12 of the unit's range, two in
+// flight, with an online softmax over them.  Both products run on the tensor
+// cores (mma.sync m16n8k16, bf16 in, fp32 accumulate):
+//   S^T [heads x keys] = Q K^T   (A = queries, rows 0..G-1 of 16; B = K rows)
+//   O^T [dims x heads] += V^T P^T (A = V tile, transposed by ldmatrix; B = the
+//                                  probabilities, taken straight from the S^T
+//                                  fragments as a bf16 pair hi + lo, so P keeps
+//                                  16 significant bits: two MMAs per tile row)
+// The mbarriers in `sm.bars` are initialised (count ATT_BAR_COUNT) by the
+// caller; `tiles_done` counts the tiles this warp consumed before (warp-
+// uniform, kept by the caller across units), which fixes buffer and parity.
+// Returns false after a timed-out copy (the device status holds the error).
 template <int G>
-__global__ void __launch_bounds__(ATT_THREADS) gqa_decode_kernel(const AttnParams p) {
-  extern __shared__ __align__(128) uint8_t smem_att[];
-  uint8_t* tiles = smem_att;                                               // [warp][buf][K | V]
-  uint16_t* q_s = reinterpret_cast<uint16_t*>(smem_att + ATT_TILES_BYTES);  // [G][128] rotated queries
-  uint16_t* knew = q_s + G * ATT_D;                                        // rotated new key
-  uint16_t* vnew = knew + ATT_D;                                           // new value
-  uint64_t* bars = reinterpret_cast<uint64_t*>(vnew + ATT_D);             // [warp][buf]
-  __shared__ int s_abort, s_last;
-
-  pdl_trigger();  // the next kernel may launch; it waits for this grid before reading
-  const int b = blockIdx.x, g = blockIdx.y, sp = blockIdx.z;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  if (tid == 0) {
-    for (int i = 0; i < ATT_WARPS * ATT_NBUF; ++i) mbar_init(&bars[i], 1);
-    s_abort = 0;
-    fence_mbar_init();
-  }
-  __syncthreads();
-  pdl_wait();
+__device__ __forceinline__ bool attn_unit(const AttnParams& p, int b, int g, int sp, const AttnSmem& sm,
+                                          uint32_t& tiles_done, int t, int bar) {
+  static_assert(G >= 1 && G <= 8, "at most 8 query heads per KV head");
+  const int lane = t & 31, warp = t >> 5;
   const int pos = p.positions[b];
   if (pos < 0 || pos >= p.max_len || pos >= p.rope_len || pos >= p.max_ctx) {
-    if (tid == 0 && sp == 0) record_error(DEV_ERR_BOUNDS, 300);
-    return;
+    if (t == 0 && sp == 0) record_error(DEV_ERR_BOUNDS, 300);
+    return true;
   }
   const int L = pos + 1;
   const int nparts = (L + ATT_SPLIT_KEYS - 1) / ATT_SPLIT_KEYS;
-  if (sp >= nparts) return;
+  if (sp >= nparts) return true;
   const int r0 = sp * ATT_SPLIT_KEYS, r1 = min(L, r0 + ATT_SPLIT_KEYS);
   const int ntiles = (r1 - r0 + ATT_TILE - 1) / ATT_TILE;
-  const int my_n = ntiles > warp ? (ntiles - warp + ATT_WARPS - 1) / ATT_WARPS : 0;  // tiles of this warp
+  const int ntw = ntiles > warp ? (ntiles - warp + ATT_WARPS - 1) / ATT_WARPS : 0;  // tiles of this warp
 
   const size_t cache_row0 = ((size_t)b * p.n_kv + g) * p.max_len;
   uint16_t* kc = p.k_cache + cache_row0 * ATT_D;
   uint16_t* vc = p.v_cache + cache_row0 * ATT_D;
+  const uint32_t td0 = tiles_done;
   auto tile_t0 = [&](int i) { return r0 + (warp + i * ATT_WARPS) * ATT_TILE; };
-  auto tile_buf = [&](int i) { return tiles + (size_t)(warp * ATT_NBUF + i % ATT_NBUF) * 2 * ATT_TILE_BYTES; };
-  auto tile_bar = [&](int i) { return &bars[warp * ATT_NBUF + i % ATT_NBUF]; };
-  // Lane 0 arms the barrier, lanes 0 / 1 copy K / V (a thread's copies run one
-  // after another, so the two go out from different lanes).
+  auto tile_buf = [&](int i) {
+    return sm.tiles + (size_t)(warp * ATT_NBUF + ((td0 + i) & 1)) * 2 * ATT_TILE_BYTES;
+  };
+  auto tile_bar = [&](int i) { return &sm.bars[warp * ATT_NBUF + ((td0 + i) & 1)]; };
+  auto tile_parity = [&](int i) { return (uint32_t)(((td0 + i) >> 1) & 1); };
+  // Every lane copies 16 of the tile's 512 16-byte chunks (K then V, 16 per
+  // row) into the swizzled layout; rows past the range are zero-filled.
   auto issue = [&](int i) {
     const int t0 = tile_t0(i), nk = min(ATT_TILE, r1 - t0);
-    if (lane == 0) mbar_arrive_expect_tx(tile_bar(i), (uint32_t)(2 * nk * ATT_D * 2));
-    __syncwarp();
-    if (lane < 2)
-      bulk_g2s(tile_buf(i) + lane * ATT_TILE_BYTES, (lane == 0 ? kc : vc) + (size_t)t0 * ATT_D,
-               (uint32_t)(nk * ATT_D * 2), tile_bar(i));
+    const uint32_t base = smem_u32(tile_buf(i));
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      const int q = lane + 32 * k;
+      const int tensor = q >> 8, row = (q >> 4) & 15, c = q & 15;
+      const bool in = row < nk;
+      const uint16_t* src = (tensor ? vc : kc) + (size_t)(t0 + (in ? row : 0)) * ATT_D + c * 8;
+      cp_async16_zfill(base + tensor * ATT_TILE_BYTES + att_swz(row, c), src, in ? 16u : 0u);
+    }
+    cp_async_arrive_noinc(tile_bar(i));
   };
-  for (int i = 0; i < min(my_n, ATT_NBUF); ++i) issue(i);
+  for (int i = 0; i < min(ntw, ATT_NBUF); ++i) issue(i);
 
   // ---- 1. RoPE on the G query heads and the new key; stage the new value ----
   const int row_elems = (p.n_heads + 2 * p.n_kv) * ATT_D;
   const uint16_t* qkv = p.qkv + (size_t)b * row_elems;
-  if (tid < ATT_D / 2) {
-    const int i = tid;
+  if (t < ATT_D / 2) {
+    const int i = t;
     const float c = bf16_bits_to_f32(p.rope_cos[(size_t)pos * (ATT_D / 2) + i]);
     const float s = bf16_bits_to_f32(p.rope_sin[(size_t)pos * (ATT_D / 2) + i]);
 #pragma unroll
@@ -131,141 +207,158 @@ __global__ void __launch_bounds__(ATT_THREADS) gqa_decode_kernel(const AttnParam
       const float x2 = bf16_bits_to_f32(src[i + 64]);
       const float o1 = round_bf16(__fadd_rn(round_bf16(__fmul_rn(x1, c)), round_bf16(__fmul_rn(-x2, s))));
       const float o2 = round_bf16(__fadd_rn(round_bf16(__fmul_rn(x2, c)), round_bf16(__fmul_rn(x1, s))));
-      uint16_t* dst = (hh < G) ? q_s + hh * ATT_D : knew;
+      uint16_t* dst = (hh < G) ? sm.qb + hh * ATT_QROW : sm.knew;
       dst[i] = f32_to_bf16_bits(o1);
       dst[i + 64] = f32_to_bf16_bits(o2);
     }
   } else {
-    const int i = tid - ATT_D / 2;  // 64 threads x 2 values
-    reinterpret_cast<uint32_t*>(vnew)[i] =
+    const int i = t - ATT_D / 2;  // 64 threads x 2 values
+    reinterpret_cast<uint32_t*>(sm.vnew)[i] =
         reinterpret_cast<const uint32_t*>(qkv + (size_t)(p.n_heads + p.n_kv + g) * ATT_D)[i];
   }
-  __syncthreads();
-  if (sp == nparts - 1 && tid < 32) {  // append row `pos` (16 B per lane: 16 lanes K, 16 lanes V)
-    const int part = tid >> 4, c = tid & 15;
+  att_sync(bar);
+  if (sp == nparts - 1 && t < 32) {  // append row `pos` (16 B per lane: 16 lanes K, 16 lanes V)
+    const int part = t >> 4, c = t & 15;
     uint16_t* dst = (part == 0 ? kc : vc) + (size_t)pos * ATT_D;
-    const uint16_t* src = part == 0 ? knew : vnew;
+    const uint16_t* src = part == 0 ? sm.knew : sm.vnew;
     reinterpret_cast<uint4*>(dst)[c] = reinterpret_cast<const uint4*>(src)[c];
   }
 
-  // ---- 2. scores, online softmax, P.V ----
-  float m_run[G], l_run[G], acc[G][4];
+  // ---- 2. this warp's tiles, online softmax ----
+  // query fragments (A operand rows = heads): dims 16 ks + 2 (lane % 4) and + 8
+  const int qr = lane >> 2, qc = 2 * (lane & 3);
+  uint32_t qa0[8], qa2[8];
 #pragma unroll
-  for (int hh = 0; hh < G; ++hh) {
-    m_run[hh] = -INFINITY;
-    l_run[hh] = 0.f;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) acc[hh][j] = 0.f;
+  for (int ks = 0; ks < 8; ++ks) {
+    qa0[ks] = qr < G ? *reinterpret_cast<const uint32_t*>(sm.qb + qr * ATT_QROW + 16 * ks + qc) : 0u;
+    qa2[ks] = qr < G ? *reinterpret_cast<const uint32_t*>(sm.qb + qr * ATT_QROW + 16 * ks + 8 + qc) : 0u;
   }
-  const int key = lane & (ATT_TILE - 1), half = lane >> 4;
-  int waited = 0;  // tiles whose copies this warp has seen land
-  for (int i = 0; i < my_n; ++i) {
+  float m_run = -INFINITY, l_run = 0.f;  // softmax state of head qr (lanes 4 qr .. 4 qr + 3)
+  // O^T fragments: m-tile mt holds dims 16 mt + qr (e 0, 1) and + 8 (e 2, 3),
+  // heads qc (e 0, 2) and qc + 1 (e 1, 3)
+  float acc[8][4];
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[j][e] = 0.f;
+  // ldmatrix row addresses: lane -> matrix lane / 8, row lane % 8
+  const int mi = lane >> 3, mr = lane & 7;
+  int done = 0;
+  bool ok = true;
+  for (int i = 0; i < ntw; ++i) {
     const int t0 = tile_t0(i), nk = min(ATT_TILE, r1 - t0);
     uint8_t* buf = tile_buf(i);
-    if (!__all_sync(0xffffffffu, mbar_wait(tile_bar(i), (uint32_t)((i / ATT_NBUF) & 1), 301))) {
-      if (lane == 0) s_abort = 1;
-      break;
-    }
-    waited = i + 1;
-    if (pos >= t0 && pos < t0 + nk) {  // the new row: take it from shared memory
-      uint32_t* kr = reinterpret_cast<uint32_t*>(buf + (pos - t0) * ATT_D * 2);
-      uint32_t* vr = reinterpret_cast<uint32_t*>(buf + ATT_TILE_BYTES + (pos - t0) * ATT_D * 2);
-      kr[lane] = reinterpret_cast<const uint32_t*>(knew)[lane];
-      kr[lane + 32] = reinterpret_cast<const uint32_t*>(knew)[lane + 32];
-      vr[lane] = reinterpret_cast<const uint32_t*>(vnew)[lane];
-      vr[lane + 32] = reinterpret_cast<const uint32_t*>(vnew)[lane + 32];
+    ok = __all_sync(0xffffffffu, mbar_wait(tile_bar(i), tile_parity(i), 301));
+    if (!ok) break;
+    if (pos >= t0 && pos < t0 + nk) {  // the new row: from shared memory
+      const int r = pos - t0, c = lane & 15;
+      const uint16_t* src = lane < 16 ? sm.knew : sm.vnew;
+      *reinterpret_cast<uint4*>(buf + (lane >> 4) * ATT_TILE_BYTES + att_swz(r, c)) =
+          reinterpret_cast<const uint4*>(src)[c];
       __syncwarp();
     }
-    // scores: lane (key, half) dots 64 dimensions; 16-byte chunks are visited in
-    // a key-rotated order so the 8 lanes of a shared-memory phase hit 8
-    // different bank groups
-    float sc[G];
+    const uint32_t kb = smem_u32(buf), vb = kb + ATT_TILE_BYTES;
+    // S^T [heads x keys]: two n-tiles of 8 keys
+    float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int hh = 0; hh < G; ++hh) sc[hh] = 0.f;
-    if (key < nk) {
-      const uint8_t* krow = buf + key * ATT_D * 2 + half * 128;
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const int ch = (c + key) & 7;
-        float kf[8];
-        bf16x8_to_f32(*reinterpret_cast<const uint4*>(krow + ch * 16), kf);
-#pragma unroll
-        for (int hh = 0; hh < G; ++hh) {
-          float qf[8];
-          bf16x8_to_f32(*reinterpret_cast<const uint4*>(q_s + hh * ATT_D + half * 64 + ch * 8), qf);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) sc[hh] = fmaf(kf[e], qf[e], sc[hh]);
-        }
-      }
+    for (int ks = 0; ks < 8; ++ks) {
+      // matrices: (keys 0-7, chunk 2ks), (keys 0-7, 2ks+1), (keys 8-15, 2ks), (keys 8-15, 2ks+1)
+      const int key = (mi >> 1) * 8 + mr;
+      uint32_t b0, b1, b2, b3;
+      ldsm_x4(kb + att_swz(key, 2 * ks + (mi & 1)), b0, b1, b2, b3);
+      mma_bf16_16816(s0, qa0[ks], qa2[ks], b0, b1);
+      mma_bf16_16816(s1, qa0[ks], qa2[ks], b2, b3);
     }
-    float pr[G];
+    // row qr, keys qc, qc+1, 8+qc, 8+qc+1
+    float sv[4] = {s0[0], s0[1], s1[0], s1[1]};
+    const int kk[4] = {qc, qc + 1, 8 + qc, 9 + qc};
+    float mx = -INFINITY;
 #pragma unroll
-    for (int hh = 0; hh < G; ++hh) {
-      const float full_dot = sc[hh] + __shfl_xor_sync(0xffffffffu, sc[hh], 16);
-      const float s = (key < nk) ? full_dot * p.scale : -INFINITY;
-      float mx = s;
-#pragma unroll
-      for (int o = ATT_TILE / 2; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-      const float m_new = fmaxf(m_run[hh], mx);
-      const float corr = expf(m_run[hh] - m_new);  // exp(-inf) = 0 on the first tile
-      const float e = (key < nk) ? expf(s - m_new) : 0.f;
-      float es = e;
-#pragma unroll
-      for (int o = ATT_TILE / 2; o > 0; o >>= 1) es += __shfl_xor_sync(0xffffffffu, es, o);
-      l_run[hh] = l_run[hh] * corr + es;
-      m_run[hh] = m_new;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) acc[hh][j] *= corr;
-      pr[hh] = e;
+    for (int e = 0; e < 4; ++e) {
+      sv[e] = kk[e] < nk ? sv[e] * p.scale : -INFINITY;
+      mx = fmaxf(mx, sv[e]);
     }
-    const uint8_t* vb = buf + ATT_TILE_BYTES + lane * 8;
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    const float m_new = fmaxf(m_run, mx);
+    const float corr = expf(m_run - m_new);  // exp(-inf) = 0 on the first tile
+    float ev[4], es = 0.f;
 #pragma unroll
-    for (int j = 0; j < ATT_TILE; ++j) {
-      if (j < nk) {
-        const uint2 vv = *reinterpret_cast<const uint2*>(vb + j * ATT_D * 2);
-        const float v0 = __uint_as_float(vv.x << 16), v1 = __uint_as_float(vv.x & 0xFFFF0000u);
-        const float v2 = __uint_as_float(vv.y << 16), v3 = __uint_as_float(vv.y & 0xFFFF0000u);
-#pragma unroll
-        for (int hh = 0; hh < G; ++hh) {
-          const float pj = __shfl_sync(0xffffffffu, pr[hh], j);
-          acc[hh][0] = fmaf(pj, v0, acc[hh][0]);
-          acc[hh][1] = fmaf(pj, v1, acc[hh][1]);
-          acc[hh][2] = fmaf(pj, v2, acc[hh][2]);
-          acc[hh][3] = fmaf(pj, v3, acc[hh][3]);
-        }
-      }
+    for (int e = 0; e < 4; ++e) {
+      ev[e] = kk[e] < nk ? expf(sv[e] - m_new) : 0.f;
+      es += ev[e];
     }
-    // Reuse the buffer: every lane is done reading it (generic proxy) before
-    // the bulk copy (async proxy) overwrites it.
+    es += __shfl_xor_sync(0xffffffffu, es, 1);
+    es += __shfl_xor_sync(0xffffffffu, es, 2);
+    l_run = l_run * corr + es;
+    m_run = m_new;
+    // rescale: this lane's accumulators belong to heads qc and qc + 1, whose
+    // state lives in lanes 4 qc and 4 qc + 4
+    const float c_lo = __shfl_sync(0xffffffffu, corr, 4 * qc);
+    const float c_hi = __shfl_sync(0xffffffffu, corr, (4 * qc + 4) & 31);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      acc[j][0] *= c_lo;
+      acc[j][1] *= c_hi;
+      acc[j][2] *= c_lo;
+      acc[j][3] *= c_hi;
+    }
+    // P^T (B operand, k = keys, n = heads) straight from the score fragments,
+    // split into bf16 hi + lo parts (the products with bf16 V are exact in fp32)
+    float eh[4], el[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      eh[e] = round_bf16(ev[e]);
+      el[e] = ev[e] - eh[e];
+    }
+    const uint32_t pb0 = pack_bf16x2(eh[0], eh[1]), pb1 = pack_bf16x2(eh[2], eh[3]);
+    const uint32_t pl0 = pack_bf16x2(el[0], el[1]), pl1 = pack_bf16x2(el[2], el[3]);
+#pragma unroll
+    for (int mt = 0; mt < 8; ++mt) {
+      // matrices (transposed): (keys 0-7, chunk 2mt), (keys 0-7, 2mt+1), (keys 8-15, 2mt), (keys 8-15, 2mt+1)
+      const int key = (mi >> 1) * 8 + mr;
+      uint32_t a0, a1, a2, a3;
+      ldsm_x4_t(vb + att_swz(key, 2 * mt + (mi & 1)), a0, a1, a2, a3);
+      mma_bf16_16816_full(acc[mt], a0, a1, a2, a3, pb0, pb1);
+      mma_bf16_16816_full(acc[mt], a0, a1, a2, a3, pl0, pl1);
+    }
+    // Reuse the buffer: every lane is done reading it before the next copies.
     __syncwarp();
-    if (i + ATT_NBUF < my_n) {
-      fence_proxy_async_smem();
-      issue(i + ATT_NBUF);
-    }
+    done = i + 1;
+    if (i + ATT_NBUF < ntw) issue(i + ATT_NBUF);
   }
-  // Copies still in flight after an abort land before shared memory is reused.
-  for (int i = waited; i < min(my_n, waited + ATT_NBUF); ++i) mbar_wait(tile_bar(i), (uint32_t)((i / ATT_NBUF) & 1), 302);
-  __syncthreads();
-  if (s_abort) return;
+  // Copies still in flight after a time-out land before the buffers are reused.
+  for (int i = done; i < min(ntw, done + ATT_NBUF); ++i) mbar_wait(tile_bar(i), tile_parity(i), 302);
+  tiles_done = td0 + (uint32_t)ntw;
+  if (!ok && lane == 0) *sm.flag = -1;
+  att_sync(bar);
+  if (*sm.flag == -1) return false;
 
   // ---- 3. merge the warp states (tile buffers are free now) ----
-  float* sm_m = reinterpret_cast<float*>(tiles);      // [warp][G]
-  float* sm_l = sm_m + ATT_WARPS * G;                 // [warp][G]
-  float* sm_acc = sm_l + ATT_WARPS * G;               // [warp][G][128]
-#pragma unroll
-  for (int hh = 0; hh < G; ++hh) {
-    if (lane == 0) {
-      sm_m[warp * G + hh] = m_run[hh];
-      sm_l[warp * G + hh] = l_run[hh];
-    }
-    *reinterpret_cast<float4*>(sm_acc + (warp * G + hh) * ATT_D + lane * 4) =
-        make_float4(acc[hh][0], acc[hh][1], acc[hh][2], acc[hh][3]);
+  float* sm_m = reinterpret_cast<float*>(sm.tiles);  // [warp][G]
+  float* sm_l = sm_m + ATT_WARPS * G;                // [warp][G]
+  float* sm_acc = sm_l + ATT_WARPS * G;              // [warp][G][128]
+  if (qr < G && (lane & 3) == 0) {
+    sm_m[warp * G + qr] = m_run;
+    sm_l[warp * G + qr] = l_run;
   }
-  __syncthreads();
+#pragma unroll
+  for (int mt = 0; mt < 8; ++mt) {
+    const int d = 16 * mt + qr;
+    if (qc < G) {
+      sm_acc[(warp * G + qc) * ATT_D + d] = acc[mt][0];
+      sm_acc[(warp * G + qc) * ATT_D + d + 8] = acc[mt][2];
+    }
+    if (qc + 1 < G) {
+      sm_acc[(warp * G + qc + 1) * ATT_D + d] = acc[mt][1];
+      sm_acc[(warp * G + qc + 1) * ATT_D + d + 8] = acc[mt][3];
+    }
+  }
+  att_sync(bar);
   uint16_t* out_b = p.out + (size_t)b * p.n_heads * ATT_D + (size_t)g * G * ATT_D;
   const size_t pf = (size_t)att_part_floats(G);
   float* part_base = p.ws_part + ((size_t)b * p.n_kv + g) * p.nsplit * pf;
-  for (int idx = tid; idx < G * ATT_D; idx += ATT_THREADS) {
+  for (int idx = t; idx < G * ATT_D; idx += ATT_THREADS) {
     const int hh = idx / ATT_D, d = idx % ATT_D;
     float M = -INFINITY;
 #pragma unroll
@@ -288,34 +381,62 @@ __global__ void __launch_bounds__(ATT_THREADS) gqa_decode_kernel(const AttnParam
       part[2 * G + idx] = num;
     }
   }
-  if (nparts == 1) return;
+  if (nparts == 1) {
+    att_sync(bar);  // shared memory is reused by the group's next unit
+    return true;
+  }
 
-  // ---- 4. the last CTA of (b, g) merges the parts ----
+  // ---- 4. the last unit of (b, g) merges the parts ----
   __threadfence();
-  __syncthreads();
-  if (tid == 0) {
+  att_sync(bar);
+  if (t == 0) {
     int* cnt = p.ws_count + (size_t)b * p.n_kv + g;
     const int old = atomicAdd(cnt, 1);
-    s_last = (old == nparts - 1);
-    if (s_last) atomicExch(cnt, 0);  // ready for the next launch
+    const int last = (old == nparts - 1);
+    if (last) atomicExch(cnt, 0);  // ready for the next launch
+    *sm.flag = last;
+  }
+  att_sync(bar);
+  const bool last = *sm.flag == 1;
+  if (last) {
+    __threadfence();
+    for (int idx = t; idx < G * ATT_D; idx += ATT_THREADS) {
+      const int hh = idx / ATT_D;
+      float M = -INFINITY;
+      for (int s = 0; s < nparts; ++s) M = fmaxf(M, __ldcg(part_base + s * pf + hh));
+      float num = 0.f, den = 0.f;
+      for (int s = 0; s < nparts; ++s) {
+        const float* part = part_base + s * pf;
+        const float ls = __ldcg(part + G + hh);
+        const float f = (ls > 0.f) ? expf(__ldcg(part + hh) - M) : 0.f;
+        num = fmaf(__ldcg(part + 2 * G + idx), f, num);
+        den = fmaf(ls, f, den);
+      }
+      out_b[idx] = f32_to_bf16_bits(num / den);
+    }
+  }
+  att_sync(bar);
+  if (t == 0) *sm.flag = 0;
+  return true;
+}
+
+// Standalone launch: grid (B, n_kv_heads, nsplit), one unit per CTA.
+template <int G>
+__global__ void __launch_bounds__(ATT_THREADS) gqa_decode_kernel(const AttnParams p) {
+  extern __shared__ __align__(128) uint8_t smem_att[];
+  __shared__ int s_flag;
+  const AttnSmem sm = att_carve(smem_att, smem_att + ATT_TILES_BYTES, G, &s_flag);
+  pdl_trigger();  // the next kernel may launch; it waits for this grid before reading
+  const int t = threadIdx.x;
+  if (t == 0) {
+    for (int i = 0; i < ATT_WARPS * ATT_NBUF; ++i) mbar_init(&sm.bars[i], ATT_BAR_COUNT);
+    s_flag = 0;
+    fence_mbar_init();
   }
   __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  for (int idx = tid; idx < G * ATT_D; idx += ATT_THREADS) {
-    const int hh = idx / ATT_D;
-    float M = -INFINITY;
-    for (int s = 0; s < nparts; ++s) M = fmaxf(M, __ldcg(part_base + s * pf + hh));
-    float num = 0.f, den = 0.f;
-    for (int s = 0; s < nparts; ++s) {
-      const float* part = part_base + s * pf;
-      const float ls = __ldcg(part + G + hh);
-      const float f = (ls > 0.f) ? expf(__ldcg(part + hh) - M) : 0.f;
-      num = fmaf(__ldcg(part + 2 * G + idx), f, num);
-      den = fmaf(ls, f, den);
-    }
-    out_b[idx] = f32_to_bf16_bits(num / den);
-  }
+  pdl_wait();
+  uint32_t tiles_done = 0;
+  attn_unit<G>(p, blockIdx.x, blockIdx.y, blockIdx.z, sm, tiles_done, t, 0);
 }
 
 }  // namespace bitnet

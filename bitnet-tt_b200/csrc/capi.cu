@@ -12,12 +12,16 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <vector>
+#include <algorithm>
+#include <cmath>
 
 #include "act_quant.cuh"
 #include "attention.cuh"
 #include "bitlinear_simt.cuh"
 #include "bitlinear_tc.cuh"
 #include "common.cuh"
+#include "decode_layers.cuh"
 #include "lm_head.cuh"
 #include "lm_head_tc.cuh"
 #include "pack.cuh"
@@ -660,4 +664,233 @@ extern "C" int bitnet_bitlinear_noalloc(const void* x, int M, int K, const void*
   int32_t* sum = reinterpret_cast<int32_t*>(base + kNoallocSumOff);
   return bitnet_bitlinear(x, M, K, gamma, eps, w_packed, N, segments, epilogue, residual, y, acc_out, q, scale, sum,
                           path, stream);
+}
+
+// ---------------------------------------------------------------------------
+// persistent decode of every layer
+// ---------------------------------------------------------------------------
+static_assert(sizeof(void*) != 8 || sizeof(bitnet_decode_layer_t) == 224, "bitnet_decode_layer_t layout");
+static_assert(sizeof(void*) != 8 || sizeof(bitnet_decode_desc_t) == 144, "bitnet_decode_desc_t layout");
+
+struct bitnet_decode_plan {
+  int device = -1;
+  int G = 0;
+  int grid = 0;
+  size_t smem = 0;
+  MkParams p;
+  void* dev_block = nullptr;  // layers | codes | split-K scratch | barrier words (one allocation)
+};
+
+namespace {
+std::atomic<unsigned long long> g_smem_mk[4];
+
+int mk_split(int NT, int KC, int grid) {
+  int best = 1;
+  for (int s = 1; s <= 8 && s <= KC; ++s)
+    if (NT * s <= grid) best = s;
+  return best;
+}
+
+template <int G>
+int mk_launch(bitnet_decode_plan* pl, cudaStream_t st) {
+  if (int e = ensure_smem(decode_layers_kernel<G>, &g_smem_mk[G == 1 ? 0 : (G == 2 ? 1 : (G == 4 ? 2 : 3))]))
+    return e;
+  cudaLaunchConfig_t cfg;
+  memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = dim3(pl->grid);
+  cfg.blockDim = dim3(MK_THREADS);
+  cfg.dynamicSmemBytes = pl->smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;  // all CTAs resident: the grid barriers rely on it
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, decode_layers_kernel<G>, pl->p);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx(decode_layers)");
+  return BITNET_OK;
+}
+
+template <int G>
+int mk_occupancy(int* blocks, size_t smem) {
+  if (int e = ensure_smem(decode_layers_kernel<G>, &g_smem_mk[G == 1 ? 0 : (G == 2 ? 1 : (G == 4 ? 2 : 3))]))
+    return e;
+  const cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks, decode_layers_kernel<G>, MK_THREADS, smem);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+  return BITNET_OK;
+}
+}  // namespace
+
+extern "C" int bitnet_decode_plan_create(const bitnet_decode_desc_t* d, bitnet_decode_plan_t** out) {
+  if (!d || !out) return BITNET_ERR_INVALID_ARGUMENT;
+  *out = nullptr;
+  DevInfo* di;
+  if (int e = device_info(&di)) return e;
+  const int L = d->num_layers, B = d->batch, H = d->hidden, F = d->intermediate, NH = d->n_heads, NKV = d->n_kv_heads;
+  if (L <= 0 || B <= 0 || B > MK_MAX_T || H <= 0 || F <= 0 || NH <= 0 || NKV <= 0 || NH % NKV != 0 ||
+      d->head_dim != ATT_D || !d->layers)
+    return BITNET_ERR_INVALID_ARGUMENT;
+  const int G = NH / NKV;
+  if (G != 1 && G != 2 && G != 4 && G != 8) return BITNET_ERR_INVALID_ARGUMENT;
+  const int AK = NH * ATT_D;  // attention output width
+  for (int k : {H, F, AK})
+    if (k % 8 != 0 || round_up(k, 64) > 8 * AQ_THREADS * AQ_MAXC) return BITNET_ERR_INVALID_ARGUMENT;
+  if (!d->hidden_state || !d->qkv || !d->attn || !d->mid || !d->positions || !d->rope_cos || !d->rope_sin)
+    return BITNET_ERR_INVALID_ARGUMENT;
+  if (!aligned(d->hidden_state, 16) || !aligned(d->qkv, 16) || !aligned(d->attn, 16) || !aligned(d->mid, 16))
+    return BITNET_ERR_ALIGNMENT;
+  int max_ctx = d->max_ctx;
+  if (max_ctx < 0 || d->max_len <= 0 || d->rope_len <= 0) return BITNET_ERR_INVALID_ARGUMENT;
+  if (max_ctx == 0) max_ctx = std::min(d->max_len, d->rope_len);
+  if (max_ctx > d->max_len || max_ctx > d->rope_len) return BITNET_ERR_INVALID_ARGUMENT;
+  const size_t att_ws = bitnet_gqa_decode_workspace_bytes(B, NH, NKV, max_ctx);
+  if (att_ws > 0 && (!d->attn_workspace || d->attn_workspace_bytes < att_ws)) return BITNET_ERR_INVALID_ARGUMENT;
+  if (att_ws > 0 && !aligned(d->attn_workspace, 16)) return BITNET_ERR_ALIGNMENT;
+
+  auto* pl = new bitnet_decode_plan();
+  cudaGetDevice(&pl->device);
+  pl->G = G;
+  MkParams& p = pl->p;
+  memset(&p, 0, sizeof(p));
+  p.L = L;
+  p.B = B;
+  p.T = act_tile_of(B);
+  p.eps = d->eps;
+  const int shapes[4][3] = {{(NH + 2 * NKV) * ATT_D, H, BITNET_EPI_NONE},
+                            {H, AK, BITNET_EPI_RESIDUAL_ADD},
+                            {2 * F, H, BITNET_EPI_RELU2_MUL},
+                            {H, F, BITNET_EPI_RESIDUAL_ADD}};
+  pl->smem = mk_smem_bytes(G);
+  int occ = 0;
+  int e = 0;
+  switch (G) {
+    case 1: e = mk_occupancy<1>(&occ, pl->smem); break;
+    case 2: e = mk_occupancy<2>(&occ, pl->smem); break;
+    case 4: e = mk_occupancy<4>(&occ, pl->smem); break;
+    default: e = mk_occupancy<8>(&occ, pl->smem); break;
+  }
+  if (e || occ < 1) {
+    delete pl;
+    return e ? e : BITNET_ERR_UNSUPPORTED_DEVICE;
+  }
+  pl->grid = di->sms;  // one CTA per SM, all resident
+  int max_nt = 1;
+  for (int i = 0; i < 4; ++i) {
+    MkBl& bl = p.bl[i];
+    bl.N = shapes[i][0];
+    bl.K = shapes[i][1];
+    bl.epi = shapes[i][2];
+    bl.KC = round_up(bl.K, 64) / 64;
+    bl.NT = round_up(bl.N, 128) / 128;
+    bl.S = d->splits[i] > 0 ? std::min(d->splits[i], bl.KC) : mk_split(bl.NT, bl.KC, pl->grid);
+    if (bl.S > 1) max_nt = std::max(max_nt, bl.NT);
+  }
+  // device block: layers | q_h | q_f | s_h rs_h s_f rs_f | acc_ws | tile_cnt | barrier words
+  const int T = p.T;
+  const size_t kph = (size_t)round_up(std::max(H, AK), 64), kpf = (size_t)round_up(F, 64);
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off = (off + bytes + 255) / 256 * 256;
+    return o;
+  };
+  const size_t o_layers = take(sizeof(MkLayer) * L);
+  const size_t o_qh = take((size_t)T * kph), o_qf = take((size_t)T * kpf);
+  const size_t o_sh = take(4 * T), o_rsh = take(4 * T), o_sf = take(4 * T), o_rsf = take(4 * T);
+  const size_t o_acc = take((size_t)max_nt * T * 128 * 4), o_cnt = take((size_t)max_nt * 4);
+  const size_t o_sync = take(256);
+  cudaError_t ce = cudaMalloc(&pl->dev_block, off);
+  if (ce != cudaSuccess) {
+    delete pl;
+    return cuda_fail(ce, "cudaMalloc(decode plan)");
+  }
+  uint8_t* base = (uint8_t*)pl->dev_block;
+  ce = cudaMemset(base, 0, off);
+  std::vector<MkLayer> layers(L);
+  for (int l = 0; l < L && ce == cudaSuccess; ++l) {
+    const bitnet_decode_layer_t& s = d->layers[l];
+    MkLayer& m = layers[l];
+    m.w[0] = s.w_qkv;
+    m.w[1] = s.w_o;
+    m.w[2] = s.w_gate_up;
+    m.w[3] = s.w_down;
+    const bitnet_segments_t* segs[4] = {&s.seg_qkv, &s.seg_o, &s.seg_gate_up, &s.seg_down};
+    for (int i = 0; i < 4; ++i) {
+      if (!m.w[i] || !aligned(m.w[i], 16)) e = BITNET_ERR_ALIGNMENT;
+      if (!e) e = to_dev_segments(segs[i], p.bl[i].N, p.bl[i].epi, &m.seg[i]);
+    }
+    m.gamma[0] = (const uint16_t*)s.input_layernorm;
+    m.gamma[1] = (const uint16_t*)s.attn_sub_norm;
+    m.gamma[2] = (const uint16_t*)s.post_attention_layernorm;
+    m.gamma[3] = (const uint16_t*)s.ffn_sub_norm;
+    for (int i = 0; i < 4; ++i)
+      if (m.gamma[i] && !aligned(m.gamma[i], 16)) e = BITNET_ERR_ALIGNMENT;
+    m.k_cache = (uint16_t*)s.k_cache;
+    m.v_cache = (uint16_t*)s.v_cache;
+    if (!m.k_cache || !m.v_cache) e = BITNET_ERR_INVALID_ARGUMENT;
+    else if (!aligned(m.k_cache, 16) || !aligned(m.v_cache, 16)) e = BITNET_ERR_ALIGNMENT;
+  }
+  if (ce == cudaSuccess && !e) ce = cudaMemcpy(base + o_layers, layers.data(), sizeof(MkLayer) * L, cudaMemcpyHostToDevice);
+  if (ce != cudaSuccess || e) {
+    cudaFree(pl->dev_block);
+    delete pl;
+    return e ? e : cuda_fail(ce, "decode plan set-up");
+  }
+  p.layers = (const MkLayer*)(base + o_layers);
+  p.hidden = (uint16_t*)d->hidden_state;
+  p.qkv = (uint16_t*)d->qkv;
+  p.attn = (uint16_t*)d->attn;
+  p.mid = (uint16_t*)d->mid;
+  p.q_h = (int8_t*)(base + o_qh);
+  p.q_f = (int8_t*)(base + o_qf);
+  p.s_h = (float*)(base + o_sh);
+  p.rs_h = (int32_t*)(base + o_rsh);
+  p.s_f = (float*)(base + o_sf);
+  p.rs_f = (int32_t*)(base + o_rsf);
+  p.acc_ws = (int32_t*)(base + o_acc);
+  p.tile_cnt = (int*)(base + o_cnt);
+  p.sync_ctr = (unsigned*)(base + o_sync);
+  p.abort_flag = (int*)(base + o_sync + 4);
+  AttnParams& a = p.att;
+  a.qkv = p.qkv;
+  a.n_heads = NH;
+  a.n_kv = NKV;
+  a.G = G;
+  a.positions = d->positions;
+  a.rope_cos = (const uint16_t*)d->rope_cos;
+  a.rope_sin = (const uint16_t*)d->rope_sin;
+  a.rope_len = d->rope_len;
+  a.max_len = d->max_len;
+  a.max_ctx = max_ctx;
+  a.nsplit = (max_ctx + ATT_SPLIT_KEYS - 1) / ATT_SPLIT_KEYS;
+  a.scale = 1.0f / sqrtf((float)ATT_D);
+  const size_t counters = ((size_t)B * NKV * sizeof(int) + 255) / 256 * 256;
+  a.ws_count = att_ws > 0 ? (int*)d->attn_workspace : nullptr;
+  a.ws_part = att_ws > 0 ? (float*)((uint8_t*)d->attn_workspace + counters) : nullptr;
+  a.out = p.attn;
+  p.att_units = B * NKV * a.nsplit;
+  *out = pl;
+  return BITNET_OK;
+}
+
+extern "C" int bitnet_decode_plan_run(bitnet_decode_plan_t* pl, bitnet_stream_t stream) {
+  if (!pl) return BITNET_ERR_INVALID_ARGUMENT;
+  int dev = -1;
+  cudaGetDevice(&dev);
+  if (dev != pl->device) return BITNET_ERR_INVALID_ARGUMENT;
+  const cudaError_t ce = cudaMemsetAsync(pl->p.sync_ctr, 0, 8, (cudaStream_t)stream);  // barrier + abort words
+  if (ce != cudaSuccess) return cuda_fail(ce, "cudaMemsetAsync(decode barrier)");
+  switch (pl->G) {
+    case 1: return mk_launch<1>(pl, (cudaStream_t)stream);
+    case 2: return mk_launch<2>(pl, (cudaStream_t)stream);
+    case 4: return mk_launch<4>(pl, (cudaStream_t)stream);
+    default: return mk_launch<8>(pl, (cudaStream_t)stream);
+  }
+}
+
+extern "C" int bitnet_decode_plan_destroy(bitnet_decode_plan_t* pl) {
+  if (!pl) return BITNET_OK;
+  cudaFree(pl->dev_block);
+  delete pl;
+  return BITNET_OK;
 }

@@ -145,6 +145,12 @@ __device__ __forceinline__ uint64_t l2_policy_evict_first() {
   return p;
 }
 
+// Barrier among the first `nthreads` threads that use barrier `id` (1..15;
+// 0 is __syncthreads).
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }

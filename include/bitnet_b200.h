@@ -179,6 +179,60 @@ int bitnet_gqa_decode_attention(const void* qkv, int B, int n_heads, int n_kv_he
                                 int rope_len, void* k_cache, void* v_cache, int max_len, int max_ctx, float scale,
                                 void* workspace, size_t workspace_bytes, void* out, bitnet_stream_t stream);
 
+/* ---- persistent decode of every layer -----------------------------------
+ * One launch runs all transformer layers of a decode step (the per-layer
+ * sequence of src/bitnet_tt/model/transformer.py:59-120 and
+ * inference/generator_batch32.py:656-811, _decode_step_batch32, up to the
+ * final norm): for each layer the input_layernorm act-quant, the fused QKV
+ * BitLinear, RoPE + KV append + GQA attention, attn_sub_norm act-quant, o_proj
+ * + residual, post_attention_layernorm act-quant, gate_up + ReLU^2 * up,
+ * ffn_sub_norm act-quant, down + residual.  Results are bit-identical to the
+ * same sequence of the per-operation entry points above.  No counterpart in
+ * the reference (there, each operation is its own device program inside the
+ * captured trace).
+ * Requirements: batch <= 32, head_dim 128, n_heads / n_kv_heads in {1,2,4,8},
+ * hidden, intermediate and n_heads*128 multiples of 8 and at most 8192,
+ * 16-byte aligned buffers; attention arguments as in
+ * bitnet_gqa_decode_attention (the caches come from the layers). */
+typedef struct {
+  const uint8_t* w_qkv;         /* packed [(n_heads + 2 n_kv) * 128, hidden], segments q | k | v */
+  const uint8_t* w_o;           /* packed [hidden, n_heads * 128] */
+  const uint8_t* w_gate_up;     /* packed [2 * intermediate, hidden], 64-row groups [32 gate | 32 up] */
+  const uint8_t* w_down;        /* packed [hidden, intermediate] */
+  bitnet_segments_t seg_qkv, seg_o, seg_gate_up, seg_down; /* per-tensor weight scales */
+  const void* input_layernorm;  /* bf16 [hidden] */
+  const void* attn_sub_norm;    /* bf16 [n_heads * 128] */
+  const void* post_attention_layernorm; /* bf16 [hidden] */
+  const void* ffn_sub_norm;     /* bf16 [intermediate] */
+  void* k_cache;                /* bf16 [batch, n_kv, max_len, 128] */
+  void* v_cache;
+} bitnet_decode_layer_t;
+
+typedef struct {
+  int num_layers, batch, hidden, intermediate, n_heads, n_kv_heads, head_dim;
+  float eps;
+  const bitnet_decode_layer_t* layers; /* host array [num_layers]; copied at plan creation */
+  void* hidden_state;           /* bf16 [batch, hidden]: the embeddings in, the last layer's output out */
+  void* qkv;                    /* bf16 [batch, (n_heads + 2 n_kv) * 128] scratch */
+  void* attn;                   /* bf16 [batch, n_heads * 128] scratch */
+  void* mid;                    /* bf16 [batch, intermediate] scratch */
+  const int32_t* positions;
+  const void* rope_cos;
+  const void* rope_sin;
+  int rope_len, max_len, max_ctx;
+  void* attn_workspace;         /* as for bitnet_gqa_decode_attention (zeroed once) */
+  size_t attn_workspace_bytes;
+  int splits[4];                /* K splits of the qkv, o, gate_up and down BitLinears (0 = automatic) */
+} bitnet_decode_desc_t;
+
+typedef struct bitnet_decode_plan bitnet_decode_plan_t;
+/* Validates the description, chooses the work split and allocates the plan's
+ * device scratch (activation codes, split-K partial sums, grid barrier). */
+int bitnet_decode_plan_create(const bitnet_decode_desc_t* desc, bitnet_decode_plan_t** plan);
+/* Enqueues one pass over all layers on `stream` (capturable in a CUDA graph). */
+int bitnet_decode_plan_run(bitnet_decode_plan_t* plan, bitnet_stream_t stream);
+int bitnet_decode_plan_destroy(bitnet_decode_plan_t* plan);
+
 /* ---- lm_head / embedding table -------------------------------------------
  * The tied embedding / lm_head matrix (src/bitnet_tt/utils/weights.py:236-246)
  * is stored once, in a tiled layout read by both the lm_head and the gather. */

@@ -46,7 +46,7 @@ def test_status_strings_and_sizes():
     assert _lib.argmax_workspace_bytes(32, 2560, 128256) == 160 * 32 * 8 + 2560 * 32 * 2
     assert lib.bitnet_packed_weight_bytes(0, 5) == 0
     # attention: no workspace up to 256 keys; else 256-byte aligned counters,
-    # then per (sequence, KV head, split) 2G + 128G floats
+    # then per (sequence, KV head, split of 256 keys) 2G + 128G floats
     assert _lib.gqa_decode_workspace_bytes(32, 20, 5, 256) == 0
     assert _lib.gqa_decode_workspace_bytes(32, 20, 5, 257) == 768 + 32 * 5 * 2 * (8 + 512) * 4
     assert _lib.gqa_decode_workspace_bytes(32, 20, 5, 4096) == 768 + 32 * 5 * 16 * (8 + 512) * 4

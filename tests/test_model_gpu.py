@@ -110,7 +110,7 @@ def test_attention_position_beyond_max_ctx_is_a_device_error(cuda):
     cos, sin = half_split_tables(d, max_len, 500000.0)
     out = torch.empty((b, nh * d), dtype=torch.bfloat16, device=cuda)
     pos = torch.tensor([3, 300], dtype=torch.int32, device=cuda)
-    _lib.gqa_decode_attention(qkv, nh, nkv, d, pos, cos.to(cuda), sin.to(cuda), kd, vd, 1.0, out, 256, None)
+    _lib.gqa_decode_attention(qkv, nh, nkv, d, pos, cos.to(cuda), sin.to(cuda), kd, vd, 1.0, out, 128, None)
     torch.cuda.synchronize()
     code, site = _lib.last_device_status()
     assert code == -1 and site == 300  # a kernel bounds check reads back as BITNET_ERR_INVALID_ARGUMENT
@@ -243,3 +243,39 @@ def test_full_width_two_layer_step_matches_oracle(cuda):
     dev_tok = gen.state.ids.cpu().numpy()
     mismatch = dev_tok != ref_tokens[:, 0]
     assert not np.any(mismatch & ~_near_tie(ref_logits[0]).numpy())
+
+
+@pytest.mark.parametrize("batch,full", [(32, False), (4, False), (32, True)])
+def test_persistent_decode_equals_per_op_path(cuda, batch, full):
+    """The all-layer persistent launch against the per-operation launches:
+    ids, hidden states, logits and KV caches bit-identical, including ragged
+    contexts past one attention split (256 keys)."""
+    from bitnet_tt import _lib
+    from bitnet_tt.config import BitNet2B4TConfig
+    from bitnet_tt.inference import Batch32Generator
+
+    cfg = BitNet2B4TConfig(num_layers=2, max_position_embeddings=512) if full else _small_cfg()
+    sd = _numpy_sd(cfg, seed=11)
+    model = _device_model(cfg, sd, cuda)
+    rng = np.random.default_rng(batch + full)
+    prompts = rng.integers(0, cfg.vocab_size, size=(batch, 3))
+    gens = [Batch32Generator(model, batch_size=batch, max_seq_len=640, keep_logits=True, persistent=p)
+            for p in (True, False)]
+    assert gens[0].persistent and not gens[1].persistent
+    pos = torch.from_numpy(rng.integers(100, 600, size=batch).astype(np.int32))
+    for g in gens:
+        g.set_context_limit(640)
+        g.prefill(prompts)
+        g.state.positions.copy_(pos)  # jump ahead: rows up to 599, up to three attention splits
+    for _ in range(3):
+        for g in gens:
+            g.step()
+        a, b = gens[0].state, gens[1].state
+        assert torch.equal(a.hidden, b.hidden)
+        assert torch.equal(a.logits, b.logits)
+        assert torch.equal(a.ids, b.ids)
+        assert torch.equal(a.positions, b.positions)
+    for ca, cb in zip(gens[0].state.caches, gens[1].state.caches):
+        assert torch.equal(ca.key_cache, cb.key_cache)
+        assert torch.equal(ca.value_cache, cb.value_cache)
+    assert _lib.last_device_status()[0] == 0
