@@ -44,10 +44,50 @@ METRIC = "batch-32 decode tok/s (BitNet-2B shape)"
 FALLBACK_HBM_GBS = 6650.0
 FALLBACK_BF16_TFLOPS = 1590.0
 
-# DRAM bytes per launch measured by ncu (dram__bytes_read.sum + dram__bytes_write.sum)
-# on the gate_up BitLinear at batch 32; see profiles/bitlinear_tc_gate_up_b32.md.
-# None until a capture of the current kernel exists.
-NCU_TRAFFIC_BYTES: dict[str, float | None] = {"bitlinear_gate_up": None, "lm_head": None}
+# DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) from one ncu
+# capture of each kernel class inside the decode step (caches flushed before the
+# captured launch); profiles/decode_step_dram_bytes_b32.md has the capture.
+# None where no capture of the current kernel exists.
+NCU_TRAFFIC_BYTES: dict[str, float | None] = {
+    "bitlinear_qkv": 2588928.0,
+    "bitlinear_o": 1934848.0,
+    "bitlinear_gate_up": 8984832.0,
+    "bitlinear_down": 4858368.0,
+    "act_quant": 192512.0,
+    "lm_head": 660284928.0,
+}
+
+# Kernel classes timed by kernel_rooflines, grouped by the kernel (template
+# instance) that runs them; the roofline line reports the group with the most
+# time per decode step.
+KERNEL_GROUPS = {
+    "bitlinear_tc_kernel<residual> (o_proj, down)": ("bitlinear_o", "bitlinear_down"),
+    "bitlinear_tc_kernel<relu2> (gate_up)": ("bitlinear_gate_up",),
+    "bitlinear_tc_kernel<none> (qkv)": ("bitlinear_qkv",),
+    "act_quant_vec_kernel": ("act_quant",),
+    "gqa_decode_kernel": ("attention",),
+    "lm_head (tile_hidden + lm_head_tc + argmax_reduce)": ("lm_head",),
+    "decode_layers_kernel": ("decode_layers",),
+}
+
+
+def roofline_groups(rl: dict, hbm_peak: float) -> dict:
+    out = {}
+    for name, members in KERNEL_GROUPS.items():
+        m = [rl[k] for k in members if k in rl]
+        if not m:
+            continue
+        ms = sum(x["ms_per_step"] for x in m)
+        counts = [x["ms_per_step"] * 1e3 / x["us_per_launch"] for x in m]
+        byts = sum(x["bytes_per_launch"] * c for x, c in zip(m, counts))
+        n = sum(counts)
+        gbs = byts / (ms * 1e-3) / 1e9
+        traffic = None
+        if all(x["traffic"] is not None for x in m):
+            traffic = sum(x["traffic"] * c for x, c in zip(m, counts)) / n
+        out[name] = {"ms_per_step": ms, "launches_per_step": n, "bytes_per_launch": byts / n,
+                     "us_per_launch": ms * 1e3 / n, "achieved_gbs": gbs, "frac": gbs / hbm_peak, "traffic": traffic}
+    return out
 
 
 def parse() -> argparse.Namespace:
@@ -397,6 +437,7 @@ def run_b200(args) -> None:
 
     # ---- per-kernel rooflines (rank 0) ----------------------------------------
     rl = kernel_rooflines(gen, args, hbm_peak) if rank == 0 else {}
+    launches_per_step = gen.launches_per_step
     gen.release_trace()
     status = _lib.last_device_status()
 
@@ -416,14 +457,15 @@ def run_b200(args) -> None:
     if rank != 0:
         return
 
-    dominant = max(rl, key=lambda k: rl[k]["ms_per_step"]) if rl else None
+    groups = roofline_groups(rl, hbm_peak) if rl else {}
+    dominant = max(groups, key=lambda k: groups[k]["ms_per_step"]) if groups else None
     roof = None
     if dominant:
-        d = rl[dominant]
+        d = groups[dominant]
         roof = {"kernel": dominant, "bound": "hbm", "achieved": round(d["achieved_gbs"], 1),
                 "peak": hbm_peak, "unit": "GB/s", "frac": round(d["frac"], 4), "traffic": d["traffic"],
                 "peak_kind": peak_kind}
-    launches = args.steps * gen.launches_per_step
+    launches = args.steps * launches_per_step
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
@@ -440,6 +482,8 @@ def run_b200(args) -> None:
                 "d2h_bytes_per_step": 4 * b},
         "gpu_launches": launches,
         "roofline": roof,
+        "roofline_groups": {k: {kk: (round(vv, 4) if isinstance(vv, float) else vv) for kk, vv in d.items()}
+                            for k, d in groups.items()},
         "roofline_kernels": {k: {kk: (round(vv, 4) if isinstance(vv, float) else vv) for kk, vv in d.items()}
                              for k, d in rl.items()},
         "cpu_baseline": cpu,
