@@ -67,6 +67,12 @@ struct TcParams {
 };
 
 __host__ __device__ __forceinline__ int tc_slot_bytes(int T) { return TC_STAGE_CHUNKS * 2048 + TC_STAGE_CHUNKS * 64 * T; }
+// K split: rank j of the cluster owns tokens [j * tok_cap, (j + 1) * tok_cap);
+// one CTA's partial sums for one owner are 128 rows x ldr int32 (ldr odd, so
+// the owner's column reads are free of bank conflicts).
+__host__ __device__ __forceinline__ int tc_tok_cap(int T, int split) { return (T + split - 1) / split; }
+__host__ __device__ __forceinline__ int tc_ldr(int T, int split) { return tc_tok_cap(T, split) | 1; }
+__host__ __device__ __forceinline__ int tc_part_bytes(int T, int split) { return 128 * tc_ldr(T, split) * 4; }
 __host__ __device__ __forceinline__ int tc_nacc(int T) { return T <= 32 ? 4 : (T <= 64 ? 2 : 1); }
 __host__ __device__ __forceinline__ int tc_nbuf(int T) {
   const int nb = (TC_TMEM_COLS - tc_nacc(T) * T) / 64;
@@ -79,6 +85,7 @@ struct TcCtrl {
   uint64_t a_full[TC_MAX_NBUF];
   uint64_t a_empty[TC_MAX_NBUF];
   uint64_t d_final;
+  uint64_t recv_full;  // split > 1: the peers' partials for this CTA's tokens have landed
   uint32_t tmem_base;
   int abort_flag;
   float scale[256];  // row_scale of the tile's tokens
@@ -86,6 +93,8 @@ struct TcCtrl {
   float fac0[256];   // w_scale / row_scale per token (gate scale for RELU2_MUL)
   float fac1[256];   // up scale / row_scale per token (RELU2_MUL)
 };
+
+static_assert(sizeof(TcCtrl) <= TC_CTRL_BYTES, "control block");
 
 template <int EPI>
 __global__ void __launch_bounds__(TC_THREADS, 1) bitlinear_tc_kernel(const TcParams p) {
@@ -118,6 +127,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) bitlinear_tc_kernel(const TcPar
       mbar_init(&ctrl->a_empty[b], NACC);
     }
     mbar_init(&ctrl->d_final, NACC);
+    mbar_init(&ctrl->recv_full, 1);
+    if (split > 1) mbar_arrive_expect_tx(&ctrl->recv_full, (uint32_t)((split - 1) * tc_part_bytes(T, split)));
     ctrl->abort_flag = 0;
     fence_mbar_init();
   }
@@ -288,12 +299,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1) bitlinear_tc_kernel(const TcPar
   }
 
   // Partial D -> the owner of each token.  Rank j of the cluster owns tokens
-  // [j * tok_cap, min(T, (j + 1) * tok_cap)).
+  // [j * tok_cap, min(T, (j + 1) * tok_cap)).  A CTA writes the partials of
+  // owner j into its own staging area and sends them with one bulk copy into
+  // owner j's receive slot (counted on the owner's recv_full barrier); its own
+  // share goes straight into its receive slot.  Scalar DSMEM stores cost ~0.2
+  // us each here; one bulk copy per owner replaces 16 of them per thread.
   const int cr = (split > 1) ? (int)cluster_ctarank() : 0;
-  const int tok_cap = (T + split - 1) / split;
-  const int ldr = tok_cap + 1;  // odd row stride: conflict-free column reads
+  const int tok_cap = tc_tok_cap(T, split);
+  const int ldr = tc_ldr(T, split);
   int* recv = reinterpret_cast<int*>(split > 1 ? ring + (size_t)nslot * slot_bytes : ring);
-  const uint32_t recv_base = smem_u32(recv);
+  int* stage = recv + (size_t)split * 128 * ldr;
   if (split > 1) cluster_wait();  // every CTA of the cluster has started
   const int used_acc = min(NACC, 2 * (kc_end - kc_begin));
   if (warp < TC_UNPACK_WARPS && !*abort_flag) {
@@ -320,19 +335,28 @@ __global__ void __launch_bounds__(TC_THREADS, 1) bitlinear_tc_kernel(const TcPar
           ++owner;
           obeg += tok_cap;
         }
-        const int idx = (cr * 128 + row) * ldr + (m - obeg);
+        const int idx = row * ldr + (m - obeg);
         if (owner == cr)
-          recv[idx] = (int)sum[j];
+          recv[(size_t)cr * 128 * ldr + idx] = (int)sum[j];
         else
-          st_shared_cluster_s32(mapa_shared(recv_base + (uint32_t)idx * 4u, (uint32_t)owner), (int)sum[j]);
+          stage[(size_t)owner * 128 * ldr + idx] = (int)sum[j];
       }
     }
   }
+  fence_proxy_async_smem();  // the staged partials are read by bulk copies
   tc_fence_before();
-  if (split > 1)
-    cluster_sync();
-  else
-    __syncthreads();
+  __syncthreads();
+  if (split > 1) {
+    if (tid < split && tid != cr && !*abort_flag) {
+      const uint32_t dst = mapa_shared(smem_u32(recv + (size_t)cr * 128 * ldr), (uint32_t)tid);
+      const uint32_t bar = mapa_shared(smem_u32(&ctrl->recv_full), (uint32_t)tid);
+      bulk_s2cluster(dst, stage + (size_t)tid * 128 * ldr, (uint32_t)tc_part_bytes(T, split), bar);
+      bulk_commit_group();
+    }
+    // Peers' copies land here even when this CTA gave up, so the wait does not
+    // depend on the abort flag (it is bounded like every wait).
+    if (!mbar_wait(&ctrl->recv_full, 0, 206)) *abort_flag = 1;
+  }
 
   const bool aborted = *abort_flag != 0;
   const int m_begin = cr * tok_cap, m_end = min(T, m_begin + tok_cap);
@@ -391,6 +415,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) bitlinear_tc_kernel(const TcPar
     }
   }
 
+  if (split > 1 && tid < split) bulk_wait_group_read0();  // outgoing copies have read the staging area
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {

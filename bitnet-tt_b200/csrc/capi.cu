@@ -187,8 +187,7 @@ int dispatch_simt(const int8_t* q, const float* rs, const int32_t* rsum, int M, 
 size_t tc_smem_bytes(int T, int nslot, int split) {
   const size_t ring = (size_t)nslot * tc_slot_bytes(T);
   const size_t stage = (size_t)128 * (T + 1) * 4;
-  const int tok_cap = (T + split - 1) / split;
-  const size_t recv = (size_t)split * 128 * (tok_cap + 1) * 4;
+  const size_t recv = (size_t)2 * split * tc_part_bytes(T, split);  // receive slots + staging
   size_t bytes = TC_CTRL_BYTES + (split > 1 ? ring + recv : (ring > stage ? ring : stage));
   // every CTA takes all 512 TMEM columns: at most one resident CTA per SM
   const size_t floor_bytes = (size_t)116 * 1024;

@@ -139,6 +139,22 @@ __device__ __forceinline__ void bulk_g2s_stream(void* smem_dst, const void* gsrc
       "l"(gsrc), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
       : "memory");
 }
+// Bulk copy from this CTA's shared memory into another CTA of the cluster
+// (dst and mbar are shared::cluster addresses from mapa); completion is counted
+// as transaction bytes on the destination CTA's barrier.
+__device__ __forceinline__ void bulk_s2cluster(uint32_t dst_cluster, const void* src, uint32_t bytes,
+                                               uint32_t mbar_cluster) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          dst_cluster),
+      "r"(smem_u32(src)), "r"(bytes), "r"(mbar_cluster)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until the sources of this thread's committed bulk copies may be reused.
+__device__ __forceinline__ void bulk_wait_group_read0() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
 __device__ __forceinline__ uint64_t l2_policy_evict_first() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
