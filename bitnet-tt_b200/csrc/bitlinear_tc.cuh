@@ -11,20 +11,20 @@
 //   D (128 x T, int32) accumulates in tensor memory.
 // acc' = sum_k c_k q_k is exact in int32; the epilogue subtracts row_sum[m].
 //
-// Warp roles (416 threads):
+// Warp roles (384 threads):
 //   warps 0-7   unpackers: warp w owns TMEM lane quarter w % 4 and half of the
 //               four 64-wide K chunks of a stage; after tcgen05.wait::st each
 //               warp arrives on the A buffer's `a_full` barrier.  A is a ring
 //               of up to 8 buffers (all of TMEM not taken by D): an MMA
 //               completes ~0.5-0.8 us after issue, so the unpackers must be
 //               able to run that far ahead;
-//   warps 8-11  MMA issuers: lane 0 of issuer i issues the stage's K steps
+//   warps 8-10  MMA issuers: lane 0 of issuer i issues the stage's K steps
 //               kk = i, i+NACC, ... into its own accumulator D_i (more than
 //               one issuing thread: one thread alone issues at most one MMA
 //               per ~36 ns, too slow at small N); each issuer commits to the
 //               A buffer's `a_empty`, the slot's `slot_free` and, at the end,
 //               `d_final`;
-//   warp 12     producer: bulk copies of packed weights and activations into a
+//   warp 11     producer: bulk copies of packed weights and activations into a
 //               ring of shared-memory slots (weights of the first slots before
 //               griddepcontrol.wait, so they overlap the previous kernel), the
 //               tile's per-token scales / row sums into shared memory, refills.
@@ -41,13 +41,16 @@ namespace bitnet {
 
 constexpr int TC_UNPACK_WARPS = 8;
 constexpr int TC_ISSUE_WARP0 = 8;
-constexpr int TC_PRODUCER_WARP = 12;
-constexpr int TC_THREADS = 13 * 32;
+constexpr int TC_PRODUCER_WARP = 11;
+// 12 warps: two CTAs then spread evenly over the SM's four sub-partitions (a
+// 13-warp CTA puts a fourth warp on one of them, and the register budget of a
+// sub-partition then admits only one CTA per SM)
+constexpr int TC_THREADS = 12 * 32;
 constexpr int TC_EPI_THREADS = TC_UNPACK_WARPS * 32;
 constexpr int TC_STAGE_CHUNKS = 4;  // 4 x 64 = 256 K positions per stage
 constexpr int TC_MAX_SLOTS = 16;
 constexpr int TC_MAX_NBUF = 8;      // A buffers in TMEM (64 columns each)
-constexpr int TC_TMEM_COLS = 512;
+constexpr int TC_TMEM_COLS = 512;       // one CTA per SM; 256 when two CTAs share an SM
 constexpr int TC_CTRL_BYTES = 5120;
 
 struct TcParams {
@@ -64,6 +67,7 @@ struct TcParams {
   int nslot;
   int split;
   int nbuf;  // A buffers in TMEM
+  int tmem_cols;  // 512 (one CTA per SM) or 256 (two)
 };
 
 __host__ __device__ __forceinline__ int tc_slot_bytes(int T) { return TC_STAGE_CHUNKS * 2048 + TC_STAGE_CHUNKS * 64 * T; }
@@ -73,9 +77,9 @@ __host__ __device__ __forceinline__ int tc_slot_bytes(int T) { return TC_STAGE_C
 __host__ __device__ __forceinline__ int tc_tok_cap(int T, int split) { return (T + split - 1) / split; }
 __host__ __device__ __forceinline__ int tc_ldr(int T, int split) { return tc_tok_cap(T, split) | 1; }
 __host__ __device__ __forceinline__ int tc_part_bytes(int T, int split) { return 128 * tc_ldr(T, split) * 4; }
-__host__ __device__ __forceinline__ int tc_nacc(int T) { return T <= 32 ? 4 : (T <= 64 ? 2 : 1); }
-__host__ __device__ __forceinline__ int tc_nbuf(int T) {
-  const int nb = (TC_TMEM_COLS - tc_nacc(T) * T) / 64;
+__host__ __device__ __forceinline__ int tc_nacc(int T) { return T <= 32 ? 3 : (T <= 64 ? 2 : 1); }
+__host__ __device__ __forceinline__ int tc_nbuf(int T, int cols = TC_TMEM_COLS) {
+  const int nb = (cols - tc_nacc(T) * T) / 64;
   return nb > TC_MAX_NBUF ? TC_MAX_NBUF : nb;
 }
 
@@ -97,7 +101,7 @@ struct TcCtrl {
 static_assert(sizeof(TcCtrl) <= TC_CTRL_BYTES, "control block");
 
 template <int EPI>
-__global__ void __launch_bounds__(TC_THREADS, 1) bitlinear_tc_kernel(const TcParams p) {
+__global__ void __launch_bounds__(TC_THREADS, 2) bitlinear_tc_kernel(const TcParams p) {
   extern __shared__ __align__(1024) uint8_t smem_tc[];
   TcCtrl* ctrl = reinterpret_cast<TcCtrl*>(smem_tc);
   uint8_t* ring = smem_tc + TC_CTRL_BYTES;
@@ -114,7 +118,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) bitlinear_tc_kernel(const TcPar
   const int rot = nstages > 0 ? (int)((blockIdx.x + blockIdx.y * 7u) % (unsigned)nstages) : 0;
   const int slot_bytes = tc_slot_bytes(T);
   const int wslot_bytes = TC_STAGE_CHUNKS * 2048;
-  const uint32_t ncols = TC_TMEM_COLS;
+  const uint32_t ncols = (uint32_t)p.tmem_cols;
   volatile int* abort_flag = &ctrl->abort_flag;
 
   if (tid == 0) {

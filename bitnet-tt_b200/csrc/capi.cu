@@ -75,6 +75,12 @@ int cuda_fail(cudaError_t e, const char* what) {
   return BITNET_ERR_CUDA;
 }
 
+int dev_index() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  return dev;
+}
+
 // Raise the dynamic shared memory limit of a kernel once per device, to the
 // per-CTA opt-in limit minus the kernel's static shared memory.
 template <typename K>
@@ -180,93 +186,68 @@ int dispatch_simt(const int8_t* q, const float* rs, const int32_t* rsum, int M, 
 
 // Shared-memory request of the tcgen05 BitLinear.  Besides the ring and the
 // epilogue buffers it has a floor that caps the number of resident CTAs per SM
-// at what tensor memory can serve at once (one CTA holding all 512 columns):
-// every resident CTA then gets its columns immediately, so a CTA of a cluster
-// can never sit in tcgen05.alloc while its peers wait for it at the cluster
-// barrier.
-size_t tc_smem_bytes(int T, int nslot, int split) {
+// at what tensor memory can serve at once (512 columns per SM): one CTA with
+// 512 columns, or two with 256.  Every resident CTA then gets its columns
+// immediately, so a CTA of a cluster can never sit in tcgen05.alloc while its
+// peers wait for it.
+size_t tc_smem_bytes(int T, int nslot, int split, int cols = TC_TMEM_COLS) {
   const size_t ring = (size_t)nslot * tc_slot_bytes(T);
   const size_t stage = (size_t)128 * (T + 1) * 4;
   const size_t recv = (size_t)2 * split * tc_part_bytes(T, split);  // receive slots + staging
   size_t bytes = TC_CTRL_BYTES + (split > 1 ? ring + recv : (ring > stage ? ring : stage));
-  // every CTA takes all 512 TMEM columns: at most one resident CTA per SM
-  const size_t floor_bytes = (size_t)116 * 1024;
+  const size_t floor_bytes = cols == 512 ? (size_t)116 * 1024 : (size_t)77 * 1024;
   return bytes < floor_bytes ? floor_bytes : bytes;
 }
+size_t tc_smem_limit(int cols) { return cols == 512 ? kMaxDynSmem : (size_t)112 * 1024; }
 
-int tc_nslot(int T, int KC, int split) {
+int tc_nslot(int T, int KC, int split, int cols = TC_TMEM_COLS) {
   const int chunks_max = (KC + split - 1) / split;
   const int stages_max = (chunks_max + TC_STAGE_CHUNKS - 1) / TC_STAGE_CHUNKS;
   int nslot = TC_MAX_SLOTS;
   if (nslot > stages_max) nslot = stages_max;
   if (nslot < 2) nslot = 2;
-  while (nslot > 2 && tc_smem_bytes(T, nslot, split) > kMaxDynSmem) --nslot;
+  while (nslot > 2 && tc_smem_bytes(T, nslot, split, cols) > tc_smem_limit(cols)) --nslot;
   return nslot;
 }
 
-// Clusters of `split` CTAs that can be resident at once (cached per device, T, split).
-template <typename K>
-int tc_max_active_clusters(K kernel, int T, int split, const DevInfo& dev) {
-  static std::atomic<int> cache[kMaxDevices][9][17];  // [device][split][T/16]
-  int devid = 0;
-  cudaGetDevice(&devid);
-  const int ti = T / 16;
-  if (devid >= kMaxDevices || ti > 16) return 0;
-  int v = cache[devid][split][ti].load();
-  if (v != 0) return v - 1;
-  cudaLaunchConfig_t cfg;
-  memset(&cfg, 0, sizeof(cfg));
-  cfg.gridDim = dim3(1, 1, split);
-  cfg.blockDim = dim3(TC_THREADS);
-  cfg.dynamicSmemBytes = tc_smem_bytes(T, tc_nslot(T, 64, split), split);
-  cudaLaunchAttribute at;
-  at.id = cudaLaunchAttributeClusterDimension;
-  at.val.clusterDim.x = 1;
-  at.val.clusterDim.y = 1;
-  at.val.clusterDim.z = (unsigned)split;
-  cfg.attrs = &at;
-  cfg.numAttrs = 1;
-  int n = 0;
-  if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess) {
-    (void)cudaGetLastError();
-    n = 0;
-  }
-  (void)dev;
-  cache[devid][split][ti].store(n + 1);
-  return n;
-}
-
+// Clusters of `split` CTAs that can be resident at once (cached per device, T, split, columns).
 template <int EPI>
 int dispatch_tc(TcParams p, int ntile_n, int ntile_m, bitnet_stream_t st, const DevInfo& dev) {
   auto k = bitlinear_tc_kernel<EPI>;
+  if (!(g_smem_tc[EPI].load() & 1ull << (dev_index() & 63))) {
+    // all of the SM's unified L1/shared storage as shared memory, so that two
+    // 256-column CTAs fit on an SM (also what the occupancy queries assume)
+    const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(carveout)");
+  }
   if (int e = ensure_smem(k, &g_smem_tc[EPI])) return e;
   const int tiles = ntile_n * ntile_m;
   int split = g_tc_split.load();
   if (split <= 0) {
+    // About 1.25 CTAs per SM: a K split cuts each CTA's chain of MMA stages,
+    // and two CTAs share an SM (256 tensor-memory columns each) when there are
+    // more CTAs than SMs.  Measured on B200 at 32 tokens: qkv 30 tiles -> 6,
+    // o_proj / down 20 tiles -> 8, gate_up 108 tiles -> 2.
     split = 1;
     if (ntile_m == 1 && p.T <= 64) {
-      int want = dev.sms / tiles;
-      if (want > 8) want = 8;
+      split = (5 * dev.sms / 4 + tiles / 2) / tiles;
       const int by_k = p.KC / 4;  // at least one full 256-wide stage per CTA
-      if (want > by_k) want = by_k;
-      // Largest split whose clusters are all co-resident in one wave (cluster
-      // sizes that do not pack into the GPCs leave a second wave behind).
-      for (int sp = want; sp > 1; --sp) {
-        if (tc_max_active_clusters(k, p.T, sp, dev) >= tiles) {
-          split = sp;
-          break;
-        }
-      }
+      if (split > by_k) split = by_k;
+      if (split > 8) split = 8;
+      if (split < 1) split = 1;
     }
   }
+  int cols = TC_TMEM_COLS;
+  if ((long)tiles * split > dev.sms && tc_nbuf(p.T, 256) >= 2) cols = 256;  // two CTAs per SM
   if (split > 8 || split > p.KC) return BITNET_ERR_INVALID_ARGUMENT;
   if (split > 1 && p.T > 64) return BITNET_ERR_INVALID_ARGUMENT;
-  const int nslot = tc_nslot(p.T, p.KC, split);
-  const size_t smem = tc_smem_bytes(p.T, nslot, split);
-  if (smem > kMaxDynSmem) return BITNET_ERR_INVALID_ARGUMENT;
+  const int nslot = tc_nslot(p.T, p.KC, split, cols);
+  const size_t smem = tc_smem_bytes(p.T, nslot, split, cols);
+  if (smem > tc_smem_limit(cols)) return BITNET_ERR_INVALID_ARGUMENT;
   p.nslot = nslot;
   p.split = split;
-  p.nbuf = tc_nbuf(p.T);
+  p.tmem_cols = cols;
+  p.nbuf = tc_nbuf(p.T, cols);
   return launch(k, dim3(ntile_n, ntile_m, split), dim3(TC_THREADS), smem, st, split, p);
 }
 
@@ -275,6 +256,7 @@ int dispatch_tc(TcParams p, int ntile_n, int ntile_m, bitnet_stream_t st, const 
 extern "C" {
 
 int bitnet_abi_version(void) { return kAbiVersion; }
+
 
 const char* bitnet_last_cuda_error(void) { return g_cuda_msg; }
 

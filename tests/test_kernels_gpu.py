@@ -172,6 +172,16 @@ def test_bitlinear_epilogues(cuda, path, epilogue, m):
     check_bitlinear(cuda, m, 256, 640, path=path, epilogue=epilogue, seed=m + path)
 
 
+@pytest.mark.parametrize("m,n,k,epilogue,split", [
+    (32, 3840, 2560, "none", 0),          # qkv shape, automatic split (more CTAs than SMs)
+    (32, 13824, 2560, "relu2_mul", 2),    # gate_up shape, 216 CTAs: two per SM, 256 TMEM columns
+    (32, 2560, 6912, "residual_add", 8),  # down shape, 160 CTAs
+    (16, 2560, 2560, "residual_add", 8),  # token tile 16
+])
+def test_bitlinear_tcgen05_decode_shapes(cuda, m, n, k, epilogue, split):
+    check_bitlinear(cuda, m, n, k, path=2, epilogue=epilogue, seed=n + k, split=split)
+
+
 @pytest.mark.parametrize("path", [1, 2])
 def test_bitlinear_config0_full_size(cuda, path):
     """x [32, 2560], W [6912, 2560] with P(0) = 0.4, scale 0.02."""
