@@ -84,7 +84,8 @@ __host__ __device__ __forceinline__ int tc_nbuf(int T, int cols = TC_TMEM_COLS) 
 }
 
 struct TcCtrl {
-  uint64_t full[TC_MAX_SLOTS];
+  uint64_t w_full[TC_MAX_SLOTS];  // the slot's packed weights have landed
+  uint64_t x_full[TC_MAX_SLOTS];  // the slot's activation codes have landed
   uint64_t slot_free[TC_MAX_SLOTS];
   uint64_t a_full[TC_MAX_NBUF];
   uint64_t a_empty[TC_MAX_NBUF];
@@ -123,7 +124,8 @@ __global__ void __launch_bounds__(TC_THREADS, 2) bitlinear_tc_kernel(const TcPar
 
   if (tid == 0) {
     for (int s = 0; s < nslot; ++s) {
-      mbar_init(&ctrl->full[s], 1);
+      mbar_init(&ctrl->w_full[s], 1);
+      mbar_init(&ctrl->x_full[s], 1);
       mbar_init(&ctrl->slot_free[s], NACC);
     }
     for (int b = 0; b < NB; ++b) {
@@ -187,16 +189,17 @@ __global__ void __launch_bounds__(TC_THREADS, 2) bitlinear_tc_kernel(const TcPar
     if (lane < pre) {
       const int s = lane;
       const int nch = stage_chunks(s), kc_s = kc0(s);
-      mbar_arrive_expect_tx(&ctrl->full[s], (uint32_t)(nch * 2048 + nch * 64 * T));
+      mbar_arrive_expect_tx(&ctrl->w_full[s], (uint32_t)(nch * 2048));
       bulk_g2s_stream(ring + (size_t)s * slot_bytes, p.w + ((size_t)nb * KC + kc_s) * 2048u, nch * 2048,
-                      &ctrl->full[s], l2_policy_evict_first());
+                      &ctrl->w_full[s], l2_policy_evict_first());
     }
     pdl_wait();
     if (lane < pre) {
       const int s = lane;
       const int nch = stage_chunks(s), kc_s = kc0(s);
+      mbar_arrive_expect_tx(&ctrl->x_full[s], (uint32_t)(nch * 64 * T));
       bulk_g2s(ring + (size_t)s * slot_bytes + wslot_bytes, p.q + (size_t)mt * T * p.Kp + (size_t)kc_s * 64 * T,
-               nch * 64 * T, &ctrl->full[s]);
+               nch * 64 * T, &ctrl->x_full[s]);
     }
     for (int i = lane; i < T; i += 32) {
       const int mg = mt * T + i;
@@ -212,15 +215,19 @@ __global__ void __launch_bounds__(TC_THREADS, 2) bitlinear_tc_kernel(const TcPar
         // the slot's previous stage (s - nslot) is fully consumed once its MMAs are done
         if (!wait(&ctrl->slot_free[slot], ((s / nslot) + 1) & 1, 200)) break;
         const int nch = stage_chunks(s), kc_s = kc0(s);
-        mbar_arrive_expect_tx(&ctrl->full[slot], (uint32_t)(nch * 2048 + nch * 64 * T));
+        mbar_arrive_expect_tx(&ctrl->w_full[slot], (uint32_t)(nch * 2048));
         bulk_g2s_stream(ring + (size_t)slot * slot_bytes, p.w + ((size_t)nb * KC + kc_s) * 2048u, nch * 2048,
-                        &ctrl->full[slot], policy);
+                        &ctrl->w_full[slot], policy);
+        mbar_arrive_expect_tx(&ctrl->x_full[slot], (uint32_t)(nch * 64 * T));
         bulk_g2s(ring + (size_t)slot * slot_bytes + wslot_bytes,
-                 p.q + (size_t)mt * T * p.Kp + (size_t)kc_s * 64 * T, nch * 64 * T, &ctrl->full[slot]);
+                 p.q + (size_t)mt * T * p.Kp + (size_t)kc_s * 64 * T, nch * 64 * T, &ctrl->x_full[slot]);
         issued = s + 1;
       }
       if (*abort_flag) {
-        for (int s = max(0, issued - nslot); s < issued; ++s) mbar_wait(&ctrl->full[s % nslot], (s / nslot) & 1, 204);
+        for (int s = max(0, issued - nslot); s < issued; ++s) {
+          mbar_wait(&ctrl->w_full[s % nslot], (s / nslot) & 1, 204);
+          mbar_wait(&ctrl->x_full[s % nslot], (s / nslot) & 1, 204);
+        }
       }
     }
     __syncwarp();
@@ -234,6 +241,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2) bitlinear_tc_kernel(const TcPar
       for (int s = 0; s < nstages; ++s) {
         const int slot = s % nslot, b = s % NB;
         if (!wait_spin(&ctrl->a_full[b], (s / NB) & 1, 201)) break;
+        if (!wait_spin(&ctrl->x_full[slot], (s / nslot) & 1, 207)) break;
         tc_fence_after();
         const uint32_t a_base = tbase + b * 64;
         const uint32_t b_base = smem_u32(ring + (size_t)slot * slot_bytes + wslot_bytes);
@@ -257,7 +265,10 @@ __global__ void __launch_bounds__(TC_THREADS, 2) bitlinear_tc_kernel(const TcPar
       const int slot = s % nslot, b = s % NB;
       bool ok = true;
       if (s >= NB) ok = wait_spin(&ctrl->a_empty[b], ((s / NB) + 1) & 1, 202);
-      if (ok) ok = wait(&ctrl->full[slot], (s / nslot) & 1, 203);
+      // weights only: the unpack does not wait for the activations (those come
+      // after griddepcontrol.wait), so the first stages unpack while the
+      // previous kernel still runs
+      if (ok) ok = wait(&ctrl->w_full[slot], (s / nslot) & 1, 203);
       if (ok) {
         const uint8_t* wsm = ring + (size_t)slot * slot_bytes;
         const uint32_t tst = tbase + ((uint32_t)(quarter * 32) << 16) + b * 64;
