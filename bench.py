@@ -107,6 +107,8 @@ def parse() -> argparse.Namespace:
     p.add_argument("--ref-budget-s", type=float, default=60.0, help="timed CPU work of --impl reference")
     p.add_argument("--decode-path", choices=["per-op", "persistent"], default="per-op",
                    help="per-op: 9 launches per layer; persistent: every layer in one launch")
+    p.add_argument("--vocab-shard", action="store_true",
+                   help="with N > 1: split the lm_head by vocabulary rows over the ranks (two NCCL gathers per step)")
     return p.parse_args()
 
 
@@ -378,8 +380,12 @@ def run_b200(args) -> None:
     t_build = time.perf_counter() - t_build
 
     b = args.batch
+    shard = args.vocab_shard and world > 1
+    import torch.distributed as dist  # noqa: F811 - only used when world > 1
+
     gen = Batch32Generator(model, batch_size=b, max_seq_len=args.max_seq_len,
-                           persistent=args.decode_path == "persistent")
+                           persistent=args.decode_path == "persistent",
+                           vocab_shard_group=dist.group.WORLD if shard else None)
     gen.set_context_limit(args.prompt_len + args.new_tokens)  # positions cycle within it
     rng = np.random.default_rng(args.seed * 1000 + rank)
     prompts = rng.integers(0, cfg.vocab_size, size=(b, args.prompt_len))
@@ -466,6 +472,20 @@ def run_b200(args) -> None:
                 "peak": hbm_peak, "unit": "GB/s", "frac": round(d["frac"], 4), "traffic": d["traffic"],
                 "peak_kind": peak_kind}
     launches = args.steps * launches_per_step
+    # Whole-step roofline: every byte a decode step must read once (2-bit weights,
+    # bf16 lm_head, the KV rows of the contexts, ~1 MB of activations ignored).
+    hcfg = model_config(args)
+    h_, f_ = hcfg.hidden_size, hcfg.intermediate_size
+    qkv_ = (hcfg.num_attention_heads + 2 * hcfg.num_key_value_heads) * hcfg.head_dim
+    w_layer = (qkv_ * h_ + h_ * hcfg.num_attention_heads * hcfg.head_dim + 2 * f_ * h_ + h_ * f_) // 4
+    ctx_mean = args.prompt_len + (args.new_tokens + 1) / 2.0  # positions cycle prompt+1 .. prompt+new
+    kv_step = b * ctx_mean * 2 * hcfg.num_key_value_heads * hcfg.head_dim * 2 * hcfg.num_layers
+    step_bytes = hcfg.num_layers * w_layer + 2 * hcfg.vocab_size * h_ + kv_step
+    step_s = ms_max / args.steps / 1000.0
+    step_roof = {"bytes_per_step": int(step_bytes), "ternary_weight_bytes": hcfg.num_layers * w_layer,
+                 "lm_head_bytes": 2 * hcfg.vocab_size * h_, "kv_bytes": int(kv_step),
+                 "achieved_gbs": round(step_bytes / step_s / 1e9, 1), "peak": hbm_peak, "unit": "GB/s",
+                 "frac": round(step_bytes / step_s / 1e9 / hbm_peak, 4), "peak_kind": peak_kind}
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
@@ -476,12 +496,15 @@ def run_b200(args) -> None:
                    "batch_per_gpu": b, "global_batch": b * world, "prompt_len": args.prompt_len,
                    "new_tokens": args.new_tokens, "layers": args.layers, "parallelism": f"dp{world} (batch split)",
                    "decode_path": args.decode_path,
+                   "lm_head": f"vocab-sharded over {world} ranks (NCCL gathers)" if args.vocab_shard and world > 1
+                   else "replicated",
                    "l2": "inputs larger than L2 (1.26 GB weights streamed per step)",
                    "model_build_s": round(t_build, 1)},
         "e2e": {"value": round(e2e_value, 1), "unit": "tok/s", "h2d_bytes_per_step": 4 * b,
                 "d2h_bytes_per_step": 4 * b},
         "gpu_launches": launches,
         "roofline": roof,
+        "step_roofline": step_roof,
         "roofline_groups": {k: {kk: (round(vv, 4) if isinstance(vv, float) else vv) for kk, vv in d.items()}
                             for k, d in groups.items()},
         "roofline_kernels": {k: {kk: (round(vv, 4) if isinstance(vv, float) else vv) for kk, vv in d.items()}

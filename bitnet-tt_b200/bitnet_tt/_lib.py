@@ -142,6 +142,9 @@ _SIGNATURES = {
     "bitnet_decode_plan_create": (_c_int, [ctypes.POINTER(DecodeDesc), ctypes.POINTER(_c_void_p)]),
     "bitnet_decode_plan_run": (_c_int, [_c_void_p, _c_void_p]),
     "bitnet_decode_plan_destroy": (_c_int, [_c_void_p]),
+    "bitnet_lm_head_argmax_shard": (
+        _c_int, [_c_void_p, _c_int, _c_int, _c_void_p, _c_int, _c_int, _c_void_p, _c_void_p, _c_void_p]),
+    "bitnet_argmax_merge_pairs": (_c_int, [_c_void_p, _c_int, _c_int, _c_void_p, _c_void_p, _c_void_p]),
     "bitnet_lm_head_bytes": (_c_size_t, [_c_int, _c_int]),
     "bitnet_pack_lm_head": (_c_int, [_c_void_p, _c_int, _c_int, _c_void_p, _c_void_p]),
     "bitnet_embed_gather": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_int, _c_int, _c_void_p, _c_void_p]),
@@ -405,3 +408,18 @@ class DecodePlan:
             self.close()
         except Exception:
             pass
+
+
+def lm_head_argmax_shard(h: torch.Tensor, w_tiled_shard: torch.Tensor, v_shard: int, vocab_offset: int,
+                         workspace: torch.Tensor, pairs_out: torch.Tensor) -> None:
+    """pairs_out: float32 [B, 2] viewed as {value, int32 index} (see the C header)."""
+    b, k = h.shape
+    check(load().bitnet_lm_head_argmax_shard(ptr(h), b, k, ptr(w_tiled_shard), v_shard, vocab_offset, ptr(workspace),
+                                             ptr(pairs_out), stream_handle()), "bitnet_lm_head_argmax_shard")
+
+
+def argmax_merge_pairs(pairs: torch.Tensor, out_ids: torch.Tensor, advance_positions: torch.Tensor | None = None) -> None:
+    """pairs: [nshard, B, 2] float32 pairs as written by lm_head_argmax_shard."""
+    nshard, b = pairs.shape[0], pairs.shape[1]
+    check(load().bitnet_argmax_merge_pairs(ptr(pairs), nshard, b, ptr(out_ids), ptr(advance_positions),
+                                           stream_handle()), "bitnet_argmax_merge_pairs")

@@ -94,7 +94,8 @@ class DecodeState:
 
 class Batch32Generator:
     def __init__(self, model, tokenizer: Any = None, enable_trace: bool = True, batch_size: int = PADDED_BATCH,
-                 max_seq_len: int = 2048, keep_logits: bool = False, persistent: bool | None = None) -> None:
+                 max_seq_len: int = 2048, keep_logits: bool = False, persistent: bool | None = None,
+                 vocab_shard_group=None) -> None:
         self.model = model
         self.device = model.device
         self.config = model.config
@@ -108,6 +109,15 @@ class Batch32Generator:
         # persistent=True: every layer in one launch (batch <= 32); default: 9 launches per layer
         self.persistent = bool(persistent) and batch_size <= PADDED_BATCH
         self.launches_per_step = 6 if self.persistent else 9 * self.config.num_layers + 5
+        # vocab_shard_group: a torch.distributed group over which the lm_head is
+        # split by vocabulary rows (batch-split multi-GPU decoding); its gathers
+        # run outside the captured graph, after each replay
+        self.vocab_shard_group = vocab_shard_group
+        self.vocab_head = None
+        if vocab_shard_group is not None:
+            if keep_logits:
+                raise ValueError("keep_logits is not available with a vocabulary-sharded lm_head")
+            self.launches_per_step += 1  # shard lm_head: tile, GEMV, pairs, merge (final norm stays)
         self.last_stats = GenerationStats()
         self.context_limit = max_seq_len
 
@@ -130,6 +140,12 @@ class Batch32Generator:
     def _ensure_state(self) -> DecodeState:
         if self.state is None:
             self.state = DecodeState(self.model, self.batch_size, self.max_seq_len, self.context_limit)
+            if self.vocab_shard_group is not None:
+                from .vocab_shard import VocabShardedLMHead
+
+                m = self.model
+                self.vocab_head = VocabShardedLMHead(m.lm_head_tiled, self.config.vocab_size, self.config.hidden_size,
+                                                     self.batch_size, self.device, self.vocab_shard_group)
             if self.keep_logits:
                 self.state.logits = torch.zeros((self.batch_size, self.config.vocab_size), dtype=torch.bfloat16,
                                                 device=self.device)
@@ -159,7 +175,8 @@ class Batch32Generator:
             _lib.act_quant(st.mid, layer.mlp.ffn_sub_norm.weight, eps, st.act_f)
             layer.mlp.down_proj.forward_into(st.act_f, b, st.hidden, residual=st.hidden)
         _lib.rmsnorm(st.hidden, m.norm.weight, eps, st.normed)
-        m.lm_head_argmax(st.normed, st.argmax_ws, st.ids, st.logits, st.positions)
+        if self.vocab_head is None:
+            m.lm_head_argmax(st.normed, st.argmax_ws, st.ids, st.logits, st.positions)
 
     def _capture_trace(self) -> None:
         """Warm every kernel once eagerly, then capture the step into a CUDA graph."""
@@ -190,6 +207,9 @@ class Batch32Generator:
             self._graph.replay()
         else:
             self._decode_step()
+        if self.vocab_head is not None:
+            st = self.state
+            self.vocab_head.step(st.normed, st.ids, st.positions)
 
     def warmup(self) -> None:
         self._ensure_state()

@@ -534,11 +534,12 @@ size_t bitnet_argmax_workspace_bytes(int B, int K, int V) {
   return lm_ws_hidden_offset(B) + (size_t)(round_up(K, 8) / 8) * lm_head_tile_T(B) * 16;
 }
 
-int bitnet_lm_head_argmax(const void* h, int B, int K, const void* w_tiled, int V, void* workspace, int32_t* out_ids,
-                          void* logits_out, int32_t* advance_positions, bitnet_stream_t stream) {
+// tile_hidden + lm_head_tc; the per-CTA pairs are left in the workspace.
+static int lm_head_pairs(const void* h, int B, int K, const void* w_tiled, int V, void* workspace, void* logits_out,
+                         bitnet_stream_t stream, int* grid_out) {
   DevInfo* d;
   if (int e = device_info(&d)) return e;
-  if (!h || !w_tiled || !workspace || !out_ids || B <= 0 || B > 256 || V <= 0 || K <= 0 || (K % 16) != 0)
+  if (!h || !w_tiled || !workspace || B <= 0 || B > 256 || V <= 0 || K <= 0 || (K % 16) != 0)
     return BITNET_ERR_INVALID_ARGUMENT;
   if (!aligned(w_tiled, 16) || !aligned(workspace, 256) || !aligned(h, 2)) return BITNET_ERR_ALIGNMENT;
   const int K8 = round_up(K, 8) / 8, ntiles = round_up(V, 128) / 128, T = lm_head_tile_T(B);
@@ -568,9 +569,37 @@ int bitnet_lm_head_argmax(const void* h, int B, int K, const void* w_tiled, int 
   p.part = part;
   p.logits = (uint16_t*)logits_out;
   const size_t smem = (size_t)lmt_ctrl_bytes() + (size_t)nslot * slot;
-  if (int e = launch(lm_head_tc_kernel, dim3(grid), dim3(LMT_THREADS), smem, stream, 1, p)) return e;
-  return launch(argmax_reduce_kernel, dim3(B), dim3(256), 0, stream, 1, (const ArgPair*)part, grid, B, out_ids,
-                advance_positions);
+  *grid_out = grid;
+  return launch(lm_head_tc_kernel, dim3(grid), dim3(LMT_THREADS), smem, stream, 1, p);
+}
+
+int bitnet_lm_head_argmax(const void* h, int B, int K, const void* w_tiled, int V, void* workspace, int32_t* out_ids,
+                          void* logits_out, int32_t* advance_positions, bitnet_stream_t stream) {
+  if (!out_ids) return BITNET_ERR_INVALID_ARGUMENT;
+  int grid = 0;
+  if (int e = lm_head_pairs(h, B, K, w_tiled, V, workspace, logits_out, stream, &grid)) return e;
+  return launch(argmax_reduce_kernel, dim3(B), dim3(256), 0, stream, 1, (const ArgPair*)workspace, grid, B, out_ids,
+                advance_positions, (ArgPair*)nullptr, 0);
+}
+
+int bitnet_lm_head_argmax_shard(const void* h, int B, int K, const void* w_tiled_shard, int V_shard,
+                                int vocab_offset, void* workspace, void* pairs_out, bitnet_stream_t stream) {
+  if (!pairs_out || vocab_offset < 0) return BITNET_ERR_INVALID_ARGUMENT;
+  if (!aligned(pairs_out, 8)) return BITNET_ERR_ALIGNMENT;
+  int grid = 0;
+  if (int e = lm_head_pairs(h, B, K, w_tiled_shard, V_shard, workspace, nullptr, stream, &grid)) return e;
+  return launch(argmax_reduce_kernel, dim3(B), dim3(256), 0, stream, 1, (const ArgPair*)workspace, grid, B,
+                (int32_t*)nullptr, (int32_t*)nullptr, (ArgPair*)pairs_out, vocab_offset);
+}
+
+int bitnet_argmax_merge_pairs(const void* pairs, int nshard, int B, int32_t* out_ids, int32_t* advance_positions,
+                              bitnet_stream_t stream) {
+  DevInfo* d;
+  if (int e = device_info(&d)) return e;
+  if (!pairs || !out_ids || nshard <= 0 || B <= 0 || B > 256) return BITNET_ERR_INVALID_ARGUMENT;
+  if (!aligned(pairs, 8)) return BITNET_ERR_ALIGNMENT;
+  return launch(argmax_reduce_kernel, dim3(B), dim3(256), 0, stream, 1, (const ArgPair*)pairs, nshard, B, out_ids,
+                advance_positions, (ArgPair*)nullptr, 0);
 }
 
 }  // extern "C"

@@ -18,10 +18,12 @@ __device__ __forceinline__ bool arg_better(float v, int i, float bv, int bi) {
   return v > bv || (v == bv && i < bi);
 }
 
-// grid = B, block = 256.
+// grid = B, block = 256.  Reduces the per-CTA (or per-shard) pairs of each
+// token; writes the token id (and advances the sequence's position) or, for a
+// vocabulary shard, the token's best (value, index + idx_offset) pair.
 __global__ void __launch_bounds__(256)
 argmax_reduce_kernel(const ArgPair* __restrict__ part, int ntiles, int B, int32_t* __restrict__ out_ids,
-                     int32_t* __restrict__ positions) {
+                     int32_t* __restrict__ positions, ArgPair* __restrict__ pair_out, int idx_offset) {
   __shared__ float sv[256];
   __shared__ int si[256];
   pdl_trigger();
@@ -47,8 +49,12 @@ argmax_reduce_kernel(const ArgPair* __restrict__ part, int ntiles, int B, int32_
     __syncthreads();
   }
   if (tid == 0) {
-    out_ids[b] = si[0];
-    if (positions != nullptr) positions[b] += 1;
+    if (pair_out != nullptr) {
+      pair_out[b] = ArgPair{sv[0], si[0] == 0x7fffffff ? si[0] : si[0] + idx_offset};
+    } else {
+      out_ids[b] = si[0];
+      if (positions != nullptr) positions[b] += 1;
+    }
   }
 }
 

@@ -258,6 +258,24 @@ int bitnet_lm_head_argmax(const void* h, int B, int K, const void* w_tiled, int 
                           int32_t* out_ids, void* logits_out, int32_t* advance_positions,
                           bitnet_stream_t stream);
 
+/* ---- vocabulary-sharded lm_head (multi-GPU, batch split) -------------------
+ * No counterpart in the reference (its lm_head runs on one device).  Rank r of
+ * N holds rows [vocab_offset, vocab_offset + V_shard) of the tiled table
+ * (bitnet_pack_lm_head of that slice).  A step gathers every rank's normed
+ * hidden rows (B = N x batch), runs the shard, gathers the per-row pairs of
+ * all ranks and merges them:
+ *   bitnet_lm_head_argmax_shard: pairs_out[b] = (best bf16 logit, global row
+ *     index) of row b over the shard; ties keep the smaller index.  8-byte
+ *     aligned [B] array of {float value; int32 index}.  Workspace as for
+ *     bitnet_lm_head_argmax (bitnet_argmax_workspace_bytes(B, K, V_shard)).
+ *   bitnet_argmax_merge_pairs: pairs [nshard][B] -> out_ids[b] = index of the
+ *     best pair (larger value, then smaller index); advances positions if
+ *     given.  The result equals bitnet_lm_head_argmax over the whole table. */
+int bitnet_lm_head_argmax_shard(const void* h, int B, int K, const void* w_tiled_shard, int V_shard,
+                                int vocab_offset, void* workspace, void* pairs_out, bitnet_stream_t stream);
+int bitnet_argmax_merge_pairs(const void* pairs, int nshard, int B, int32_t* out_ids, int32_t* advance_positions,
+                              bitnet_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

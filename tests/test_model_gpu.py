@@ -279,3 +279,36 @@ def test_persistent_decode_equals_per_op_path(cuda, batch, full):
         assert torch.equal(ca.key_cache, cb.key_cache)
         assert torch.equal(ca.value_cache, cb.value_cache)
     assert _lib.last_device_status()[0] == 0
+
+
+@pytest.mark.parametrize("b,nshard", [(32, 3), (64, 8), (4, 2)])
+def test_vocab_sharded_lm_head_equals_unsharded(cuda, b, nshard):
+    """Shard kernels + pair merge (what each rank of a vocabulary-split run
+    does) against the single-table lm_head + argmax: identical ids."""
+    from bitnet_tt import _lib
+    from bitnet_tt.inference.vocab_shard import shard_bounds
+
+    v, k = 1000, 512
+    g = torch.Generator().manual_seed(b * 7 + nshard)
+    h = torch.randn((b, k), generator=g).to(torch.bfloat16).to(cuda)
+    e = (0.05 * torch.randn((v, k), generator=g)).to(torch.bfloat16)
+    e[777] = e[5]  # an exact tie across shards: the smaller index must win
+    h[1] = 0       # a row where every logit ties
+    tiled = _lib.pack_lm_head(e.to(cuda))
+    ws = torch.zeros(_lib.argmax_workspace_bytes(b, k, v), dtype=torch.uint8, device=cuda)
+    ref = torch.empty(b, dtype=torch.int32, device=cuda)
+    _lib.lm_head_argmax(h, tiled, v, ws, ref)
+    pairs = torch.zeros((nshard, b, 2), dtype=torch.float32, device=cuda)
+    tile_bytes = (k // 8) * 2048
+    for r in range(nshard):
+        t0, t1, r0, rows = shard_bounds(v, nshard, r)
+        wsr = torch.zeros(_lib.argmax_workspace_bytes(b, k, max(rows, 1)), dtype=torch.uint8, device=cuda)
+        _lib.lm_head_argmax_shard(h, tiled[t0 * tile_bytes:t1 * tile_bytes], rows, r0, wsr, pairs[r])
+    ids = torch.empty(b, dtype=torch.int32, device=cuda)
+    pos = torch.zeros(b, dtype=torch.int32, device=cuda)
+    _lib.argmax_merge_pairs(pairs, ids, pos)
+    torch.cuda.synchronize()
+    assert _lib.last_device_status()[0] == 0
+    assert torch.equal(ids, ref)
+    assert int(ids[1]) == 0
+    assert torch.equal(pos.cpu(), torch.ones(b, dtype=torch.int32))
