@@ -105,6 +105,8 @@ def parse() -> argparse.Namespace:
     p.add_argument("--e2e-steps", type=int, default=256)
     p.add_argument("--cpu-baseline-steps", type=int, default=2, help="0 disables the CPU baseline")
     p.add_argument("--ref-budget-s", type=float, default=60.0, help="timed CPU work of --impl reference")
+    p.add_argument("--prefill-len", type=int, default=512,
+                   help="config 3: time a batched prefill of --batch prompts of this length (0: skip)")
     p.add_argument("--decode-path", choices=["per-op", "persistent"], default="per-op",
                    help="per-op: 9 launches per layer; persistent: every layer in one launch")
     p.add_argument("--vocab-shard", action="store_true",
@@ -362,6 +364,86 @@ def kernel_rooflines(gen, args, hbm_peak: float) -> dict:
     return res
 
 
+def prefill_measure(model, args, device, reps: int = 3) -> dict:
+    """one batched prefill of --batch prompts of --prefill-len
+    uniform random ids through the full model (TTFT).  device_ms: CUDA events
+    around the prefill enqueue (prompt ids uploaded inside); ttft_ms: host wall
+    clock from the prompt table on the host to the first generated ids on the
+    host.  The BitLinear and attention classes are then timed alone (graphs of
+    the prefill's own launches over all layers) for their tensor-pipe rates."""
+    from bitnet_tt import _lib
+    from bitnet_tt.inference import Batch32Generator
+
+    cfg = model.config
+    b, plen = args.batch, args.prefill_len
+    n = b * plen
+    gen = Batch32Generator(model, batch_size=b, max_seq_len=plen + 64)
+    gen.set_context_limit(plen + 1)
+    prompts = np.random.default_rng(args.seed + 17).integers(0, cfg.vocab_size, size=(b, plen))
+    gen.prefill(prompts)  # allocations, decode-graph capture, first launches
+    torch.cuda.synchronize(device)
+    if _lib.last_device_status()[0] != 0:
+        raise RuntimeError(f"device status {_lib.last_device_status()} after prefill warm-up")
+    dev_ms, wall_ms = [], []
+    for _ in range(reps):
+        gen.reset()
+        torch.cuda.synchronize(device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        gen._prefill_batched(prompts)
+        e1.record()
+        torch.cuda.synchronize(device)
+        dev_ms.append(e0.elapsed_time(e1))
+    for _ in range(reps):
+        gen.reset()
+        torch.cuda.synchronize(device)
+        t0 = time.perf_counter()
+        gen._prefill_batched(prompts)
+        first = gen.state.ids.cpu()
+        wall_ms.append((time.perf_counter() - t0) * 1e3)
+    assert first.numel() == b
+
+    pb, st, m = gen.prefill_buffers, gen.state, gen.model
+    h, f = cfg.hidden_size, cfg.intermediate_size
+    nq, nkv, d = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
+    qkv_n = (nq + 2 * nkv) * d
+    nl = len(m.layers)
+    lin_ops = 2 * n * nl * (qkv_n * h + h * nq * d + 2 * f * h + h * f)
+    g = graph_of(lambda: [(L.self_attn.qkv_proj.forward_into(pb.act_h, n, pb.qkv),
+                           L.self_attn.o_proj.forward_into(pb.act_h, n, pb.attn),
+                           L.mlp.gate_up_proj.forward_into(pb.act_h, n, pb.mid),
+                           L.mlp.down_proj.forward_into(pb.act_f, n, pb.hidden)) for L in m.layers], device)
+    lin_ms = time_graph(g, 3)
+    del g
+    att_flops = 4 * d * b * nq * nl * plen * (plen + 1) // 2  # QK^T and PV over the causal triangle
+    g = graph_of(lambda: [_lib.attention_prefill(pb.q, c.key_cache, c.value_cache, b, plen, nq, nkv,
+                                                 d ** -0.5, pb.attn) for c in st.caches], device)
+    att_ms = time_graph(g, 3)
+    del g
+    gen.release_trace()
+    gen.release_prefill_buffers()
+    int8_peak = 2 * FALLBACK_BF16_TFLOPS
+    bf16_peak = FALLBACK_BF16_TFLOPS
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as fh:
+            bf16_peak = float(json.load(fh)["bf16_tflops"])
+            int8_peak = 2 * bf16_peak
+    except (OSError, KeyError, ValueError):
+        pass
+    dev = statistics.median(dev_ms)
+    return {
+        "workload": f"config3: batched prefill of {b} prompts x {plen} uniform random ids, {nl} layers",
+        "tokens": n, "ttft_ms": round(statistics.median(wall_ms), 3), "device_ms": round(dev, 3),
+        "prompt_tok_s": round(n / (dev / 1e3), 1),
+        "bitlinear": {"ms": round(lin_ms, 3), "int_ops": lin_ops, "achieved_tops": round(lin_ops / lin_ms / 1e9, 1),
+                      "peak_tops": int8_peak, "frac": round(lin_ops / lin_ms / 1e9 / int8_peak, 4),
+                      "peak_kind": "int8 dense = 2 x measured bf16 GEMM burst"},
+        "attention": {"ms": round(att_ms, 3), "flops": att_flops, "achieved_tflops": round(att_flops / att_ms / 1e9, 1),
+                      "peak_tflops": bf16_peak, "frac": round(att_flops / att_ms / 1e9 / bf16_peak, 4),
+                      "peak_kind": "measured bf16 GEMM burst"},
+    }
+
+
 def run_b200(args) -> None:
     world, rank, local = dist_setup(args)
     device = torch.device("cuda", local)
@@ -445,10 +527,16 @@ def run_b200(args) -> None:
     rl = kernel_rooflines(gen, args, hbm_peak) if rank == 0 else {}
     launches_per_step = gen.launches_per_step
     gen.release_trace()
+    prefill = None
+    if rank == 0 and args.prefill_len > 0 and not shard:
+        del gen
+        torch.cuda.empty_cache()
+        prefill = prefill_measure(model, args, device)
     status = _lib.last_device_status()
 
     cpu = None
     if rank == 0 and world == 1 and args.cpu_baseline_steps > 0:
+        gen = None
         del gen, model
         torch.cuda.empty_cache()
         r = cpu_decode_sample(args, args.cpu_baseline_steps)
@@ -509,6 +597,7 @@ def run_b200(args) -> None:
                             for k, d in groups.items()},
         "roofline_kernels": {k: {kk: (round(vv, 4) if isinstance(vv, float) else vv) for kk, vv in d.items()}
                              for k, d in rl.items()},
+        "prefill": prefill,
         "cpu_baseline": cpu,
         "clocks": {k: v for k, v in clocks.summary().items()},
         "device_status": status[0],

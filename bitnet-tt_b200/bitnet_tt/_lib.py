@@ -145,6 +145,12 @@ _SIGNATURES = {
     "bitnet_lm_head_argmax_shard": (
         _c_int, [_c_void_p, _c_int, _c_int, _c_void_p, _c_int, _c_int, _c_void_p, _c_void_p, _c_void_p]),
     "bitnet_argmax_merge_pairs": (_c_int, [_c_void_p, _c_int, _c_int, _c_void_p, _c_void_p, _c_void_p]),
+    "bitnet_rope_append_prefill": (
+        _c_int, [_c_void_p, _c_int, _c_int, _c_int, _c_int, _c_int, _c_void_p, _c_void_p, _c_int, _c_void_p, _c_void_p,
+                 _c_void_p, _c_int, _c_void_p]),
+    "bitnet_attention_prefill": (
+        _c_int, [_c_void_p, _c_void_p, _c_void_p, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_float, _c_void_p,
+                 _c_void_p]),
     "bitnet_lm_head_bytes": (_c_size_t, [_c_int, _c_int]),
     "bitnet_pack_lm_head": (_c_int, [_c_void_p, _c_int, _c_int, _c_void_p, _c_void_p]),
     "bitnet_embed_gather": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_int, _c_int, _c_void_p, _c_void_p]),
@@ -423,3 +429,17 @@ def argmax_merge_pairs(pairs: torch.Tensor, out_ids: torch.Tensor, advance_posit
     nshard, b = pairs.shape[0], pairs.shape[1]
     check(load().bitnet_argmax_merge_pairs(ptr(pairs), nshard, b, ptr(out_ids), ptr(advance_positions),
                                            stream_handle()), "bitnet_argmax_merge_pairs")
+
+
+def rope_append_prefill(qkv: torch.Tensor, b: int, p: int, n_heads: int, n_kv: int, rope_cos: torch.Tensor,
+                        rope_sin: torch.Tensor, q_out: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor) -> None:
+    check(load().bitnet_rope_append_prefill(ptr(qkv), b, p, n_heads, n_kv, 128, ptr(rope_cos), ptr(rope_sin),
+                                            rope_cos.shape[0], ptr(q_out), ptr(k_cache), ptr(v_cache),
+                                            k_cache.shape[2], stream_handle()), "bitnet_rope_append_prefill")
+
+
+def attention_prefill(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, b: int, p: int, n_heads: int,
+                      n_kv: int, scale: float, out: torch.Tensor) -> None:
+    check(load().bitnet_attention_prefill(ptr(q), ptr(k_cache), ptr(v_cache), b, p, n_heads, n_kv, 128,
+                                          k_cache.shape[2], float(scale), ptr(out), stream_handle()),
+          "bitnet_attention_prefill")

@@ -11,8 +11,12 @@ substance:
     lm_head + argmax); its input (token ids) and position counters live on the
     device, the argmax kernel writes the next ids in place and advances the
     positions, so graph replays chain without host work;
-  * the prompt is consumed by the same graph, one token per replay
-    (prefill by decode), before the timed decode.
+  * prompts of one length go through a batched prefill (all B*L tokens per
+    kernel: tcgen05 BitLinear tiles of 256 tokens, causal prompt attention),
+    the reference's _prefill_batch32 (generator_batch32.py:1242-1279) without
+    the copy into a separate batch-32 cache (1281-1353): the prefill writes
+    the decode caches directly.  The part of a ragged prompt beyond the
+    shortest one is consumed by the decode graph, one token per replay.
 """
 
 from __future__ import annotations
@@ -92,6 +96,31 @@ class DecodeState:
         return sum(c.key_cache.numel() * 2 * 2 for c in self.caches)
 
 
+class PrefillBuffers:
+    """Activations of a batched prefill of `tokens` = B * L prompt tokens."""
+
+    def __init__(self, model, tokens: int):
+        cfg = model.config
+        dev = model.device
+        h, f = cfg.hidden_size, cfg.intermediate_size
+        nq, nkv, d = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
+        self.tokens = tokens
+        self.ids = torch.zeros(tokens, dtype=torch.int32, device=dev)
+        self.hidden = torch.zeros((tokens, h), dtype=torch.bfloat16, device=dev)
+        self.qkv = torch.zeros((tokens, (nq + 2 * nkv) * d), dtype=torch.bfloat16, device=dev)
+        self.q = torch.zeros((tokens, nq * d), dtype=torch.bfloat16, device=dev)
+        self.attn = torch.zeros((tokens, nq * d), dtype=torch.bfloat16, device=dev)
+        self.mid = torch.zeros((tokens, f), dtype=torch.bfloat16, device=dev)
+        self.act_h = _lib.ActBuffers(tokens, h, dev)
+        self.act_f = _lib.ActBuffers(tokens, f, dev)
+
+    def nbytes(self) -> int:
+        ts = [self.ids, self.hidden, self.qkv, self.q, self.attn, self.mid]
+        for a in (self.act_h, self.act_f):
+            ts += [a.q, a.row_scale, a.row_sum]
+        return sum(t.numel() * t.element_size() for t in ts)
+
+
 class Batch32Generator:
     def __init__(self, model, tokenizer: Any = None, enable_trace: bool = True, batch_size: int = PADDED_BATCH,
                  max_seq_len: int = 2048, keep_logits: bool = False, persistent: bool | None = None,
@@ -120,6 +149,9 @@ class Batch32Generator:
             self.launches_per_step += 1  # shard lm_head: tile, GEMV, pairs, merge (final norm stays)
         self.last_stats = GenerationStats()
         self.context_limit = max_seq_len
+        self.prefill_buffers: PrefillBuffers | None = None
+        # batched_prefill=False: every prompt token goes through the decode graph
+        self.batched_prefill = True
 
     def set_context_limit(self, n: int) -> None:
         """Bound the positions the next steps reach (positions + 1 <= n).  The
@@ -237,10 +269,54 @@ class Batch32Generator:
             raise ValueError("token id out of range")
         return prompts
 
+    def release_prefill_buffers(self) -> None:
+        self.prefill_buffers = None
+
+    def _prefill_batched(self, table: np.ndarray) -> None:
+        """All tokens of equal-length prompts table [B, L] in one pass per layer
+        (reference model/bitnet.py:217-313, mode "prefill"); writes cache rows
+        0 .. L-1 of every sequence, then the lm_head + argmax of the last
+        tokens leaves the first generated ids in st.ids and L in st.positions.
+        Enqueued on the current stream; the host does not wait."""
+        st = self.state
+        m, cfg = self.model, self.config
+        b, plen = table.shape
+        n = b * plen
+        eps = cfg.rms_norm_eps
+        nq, nkv = cfg.num_attention_heads, cfg.num_key_value_heads
+        if self.prefill_buffers is None or self.prefill_buffers.tokens != n:
+            self.prefill_buffers = None
+            self.prefill_buffers = PrefillBuffers(m, n)
+        pb = self.prefill_buffers
+        pb.ids.copy_(torch.from_numpy(np.ascontiguousarray(table, dtype=np.int32).reshape(-1)))
+        m.embed_tokens.gather_into(pb.ids, pb.hidden)
+        for layer, cache in zip(m.layers, st.caches):
+            attn = layer.self_attn
+            _lib.act_quant(pb.hidden, layer.input_layernorm.weight, eps, pb.act_h)
+            attn.qkv_proj.forward_into(pb.act_h, n, pb.qkv)
+            _lib.rope_append_prefill(pb.qkv, b, plen, nq, nkv, st.rope_cos, st.rope_sin, pb.q, cache.key_cache,
+                                     cache.value_cache)
+            _lib.attention_prefill(pb.q, cache.key_cache, cache.value_cache, b, plen, nq, nkv, attn.scale, pb.attn)
+            _lib.act_quant(pb.attn, attn.attn_sub_norm.weight, eps, pb.act_h)
+            attn.o_proj.forward_into(pb.act_h, n, pb.hidden, residual=pb.hidden)
+            _lib.act_quant(pb.hidden, layer.post_attention_layernorm.weight, eps, pb.act_h)
+            layer.mlp.gate_up_proj.forward_into(pb.act_h, n, pb.mid)
+            _lib.act_quant(pb.mid, layer.mlp.ffn_sub_norm.weight, eps, pb.act_f)
+            layer.mlp.down_proj.forward_into(pb.act_f, n, pb.hidden, residual=pb.hidden)
+        last = pb.hidden.view(b, plen, -1)[:, plen - 1]  # row stride plen * hidden
+        _lib.rmsnorm(last, m.norm.weight, eps, st.normed)
+        st.positions.fill_(plen - 1)
+        if self.vocab_head is None:
+            m.lm_head_argmax(st.normed, st.argmax_ws, st.ids, st.logits, st.positions)
+        else:
+            self.vocab_head.step(st.normed, st.ids, st.positions)
+
     def prefill(self, input_ids) -> np.ndarray:
-        """Run every prompt token through the decode step (ragged prompts allowed).
-        Returns the prompt lengths; afterwards st.ids holds each sequence's first
-        generated token and st.positions its next position."""
+        """Consume the prompts (ragged prompts allowed).  The first min(len)
+        tokens of every prompt go through the batched prefill; the rest, per
+        sequence, through the decode step one token at a time.  Returns the
+        prompt lengths; afterwards st.ids holds each sequence's first generated
+        token and st.positions its next position."""
         prompts = self._prompts(input_ids)
         lens = np.array([p.size for p in prompts])
         if int(lens.max()) >= self.max_seq_len:
@@ -250,13 +326,19 @@ class Batch32Generator:
         self.warmup()
         self.reset()
         st = self.state
-        lmax = int(lens.max())
+        lmax, lmin = int(lens.max()), int(lens.min())
+        t0 = 0
+        if self.batched_prefill:
+            self._prefill_batched(np.stack([p[:lmin] for p in prompts]))
+            if lmin == lmax:
+                return lens
+            t0 = lmin  # st.ids holds the first generated ids of the shortest prompts
         table = np.zeros((lmax, self.batch_size), dtype=np.int32)
         for b, p in enumerate(prompts):
             table[: p.size, b] = p
         table_d = torch.from_numpy(table).to(self.device)
         lens_d = torch.from_numpy(lens.astype(np.int32)).to(self.device)
-        for t in range(lmax):
+        for t in range(t0, lmax):
             # a sequence whose prompt is exhausted keeps its generated token
             st.ids.copy_(torch.where(lens_d > t, table_d[t], st.ids))
             self.step()

@@ -1,0 +1,266 @@
+// Prefill (prompt) path of the attention: RoPE + KV-cache write for all prompt
+// positions, then causal GQA attention over the prompt.
+//
+// rope_append_prefill_kernel: one thread per (token, head, pair of dims
+// (i, i + 64)); the same bf16 op-by-op half-split RoPE as the decode kernel:
+//     out[i]    = bf16(bf16(x[i] * cos_i)    + bf16(-x[i+64] * sin_i))
+//     out[i+64] = bf16(bf16(x[i+64] * cos_i) + bf16( x[i]    * sin_i))
+// Rotated queries go to q_out [B*P, n_heads*128]; rotated keys and the values
+// go to the caches at rows p = 0 .. P-1.
+//
+// attention_prefill_kernel: CTA = (query block of 64 tokens, query head, sequence),
+// 4 warps of 16 query rows.  Key blocks of 64 up to the diagonal: K and V rows
+// arrive by per-lane cp.async into the XOR-swizzled layout of the decode
+// kernel (two blocks in flight); S = Q K^T and O += P V run on mma.sync
+// m16n8k16 (bf16 in, fp32 accumulate; P as a bf16 hi + lo pair); online
+// softmax in fp32; causal mask key > query.
+#pragma once
+#include "attention.cuh"
+#include "common.cuh"
+
+namespace bitnet {
+
+constexpr int APF_THREADS = 128;  // 4 warps x 16 query rows
+constexpr int APF_QB = 64;        // query rows per CTA
+constexpr int APF_KB = 64;        // keys per block
+constexpr int APF_KV_BYTES = APF_KB * ATT_D * 2;  // K (or V) of one key block: 16 KB
+constexpr int APF_NBUF = 2;
+constexpr size_t APF_SMEM = (size_t)APF_NBUF * 2 * APF_KV_BYTES + 64;  // K|V x 2 buffers + 2 mbarriers
+
+struct RopePrefillParams {
+  const uint16_t* qkv;  // [B*P, (n_heads + 2 n_kv) * 128]
+  int B, P, n_heads, n_kv;
+  const uint16_t* rope_cos;  // [>= P, 64]
+  const uint16_t* rope_sin;
+  uint16_t* q_out;     // [B*P, n_heads * 128]
+  uint16_t* k_cache;   // [B, n_kv, max_len, 128]
+  uint16_t* v_cache;
+  int max_len;
+};
+
+__global__ void __launch_bounds__(256) rope_append_prefill_kernel(const RopePrefillParams p) {
+  pdl_trigger();
+  pdl_wait();
+  const int nh = p.n_heads + p.n_kv;  // heads that get a rotation
+  const size_t total = (size_t)p.B * p.P * nh * 64;
+  for (size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += (size_t)gridDim.x * blockDim.x) {
+    const int i = (int)(idx % 64);
+    const size_t th = idx / 64;
+    const int hh = (int)(th % nh);
+    const size_t tok = th / nh;
+    const int pos = (int)(tok % p.P);
+    const int b = (int)(tok / p.P);
+    const uint16_t* row = p.qkv + tok * (size_t)((p.n_heads + 2 * p.n_kv) * ATT_D);
+    const uint16_t* src = row + (size_t)hh * ATT_D;
+    const float c = bf16_bits_to_f32(p.rope_cos[(size_t)pos * 64 + i]);
+    const float s = bf16_bits_to_f32(p.rope_sin[(size_t)pos * 64 + i]);
+    const float x1 = bf16_bits_to_f32(src[i]);
+    const float x2 = bf16_bits_to_f32(src[i + 64]);
+    const uint16_t o1 = f32_to_bf16_bits(round_bf16(__fadd_rn(round_bf16(__fmul_rn(x1, c)), round_bf16(__fmul_rn(-x2, s)))));
+    const uint16_t o2 = f32_to_bf16_bits(round_bf16(__fadd_rn(round_bf16(__fmul_rn(x2, c)), round_bf16(__fmul_rn(x1, s)))));
+    if (hh < p.n_heads) {
+      uint16_t* dst = p.q_out + tok * (size_t)(p.n_heads * ATT_D) + (size_t)hh * ATT_D;
+      dst[i] = o1;
+      dst[i + 64] = o2;
+    } else {
+      const int g = hh - p.n_heads;
+      const size_t crow = (((size_t)b * p.n_kv + g) * p.max_len + pos) * ATT_D;
+      p.k_cache[crow + i] = o1;
+      p.k_cache[crow + i + 64] = o2;
+      const uint16_t* vsrc = row + (size_t)(p.n_heads + p.n_kv + g) * ATT_D;
+      p.v_cache[crow + i] = vsrc[i];
+      p.v_cache[crow + i + 64] = vsrc[i + 64];
+    }
+  }
+}
+
+struct AttnPrefillParams {
+  const uint16_t* q;  // [B*P, n_heads*128] rotated
+  const uint16_t* k_cache;
+  const uint16_t* v_cache;
+  int B, P, n_heads, n_kv, max_len;
+  float scale;
+  uint16_t* out;  // [B*P, n_heads*128]
+};
+
+// grid (ceil(P / 64), n_heads, B), 128 threads, APF_SMEM dynamic shared memory.
+__global__ void __launch_bounds__(APF_THREADS) attention_prefill_kernel(const AttnPrefillParams p) {
+  extern __shared__ __align__(128) uint8_t smem_apf[];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem_apf + APF_NBUF * 2 * APF_KV_BYTES);
+  pdl_trigger();
+  const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const int G = p.n_heads / p.n_kv, g = h / G;
+  if (t == 0) {
+    for (int i = 0; i < APF_NBUF; ++i) mbar_init(&bars[i], APF_THREADS);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  pdl_wait();
+  const int q0 = qb * APF_QB;
+  const int qend = min(p.P, q0 + APF_QB);            // query rows of the CTA: [q0, qend)
+  const int nkb = (qend - 1) / APF_KB + 1;           // key blocks 0 .. the one holding the last query
+  const size_t crow0 = ((size_t)b * p.n_kv + g) * p.max_len;
+  const uint16_t* kc = p.k_cache + crow0 * ATT_D;
+  const uint16_t* vc = p.v_cache + crow0 * ATT_D;
+
+  // every thread copies 2 x 64 rows x 16 chunks / 128 = 16 chunks of 16 B per block
+  auto issue = [&](int kb) {
+    const int k0 = kb * APF_KB;
+    const uint32_t base = smem_u32(smem_apf + (size_t)(kb % APF_NBUF) * 2 * APF_KV_BYTES);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int q = t + APF_THREADS * j;  // 0 .. 2047
+      const int tensor = q >> 10, row = (q >> 4) & 63, c = q & 15;
+      const bool in = k0 + row < p.P;
+      const uint16_t* src = (tensor ? vc : kc) + (size_t)(k0 + (in ? row : 0)) * ATT_D + c * 8;
+      cp_async16_zfill(base + tensor * APF_KV_BYTES + att_swz(row, c), src, in ? 16u : 0u);
+    }
+    cp_async_arrive_noinc(&bars[kb % APF_NBUF]);
+  };
+  for (int kb = 0; kb < min(nkb, APF_NBUF); ++kb) issue(kb);
+
+  // query fragments: rows q0 + 16 warp + (lane / 4) (+ 8), dims 16 ks + 2 (lane % 4) (+ 8)
+  const int qr = lane >> 2, qc = 2 * (lane & 3);
+  const int row_a = q0 + warp * 16 + qr, row_b = row_a + 8;
+  uint32_t qa[8][4];
+  {
+    const uint16_t* qa_row = p.q + ((size_t)b * p.P + min(row_a, p.P - 1)) * (size_t)(p.n_heads * ATT_D) + h * ATT_D;
+    const uint16_t* qb_row = p.q + ((size_t)b * p.P + min(row_b, p.P - 1)) * (size_t)(p.n_heads * ATT_D) + h * ATT_D;
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      qa[ks][0] = *reinterpret_cast<const uint32_t*>(qa_row + 16 * ks + qc);
+      qa[ks][1] = *reinterpret_cast<const uint32_t*>(qb_row + 16 * ks + qc);
+      qa[ks][2] = *reinterpret_cast<const uint32_t*>(qa_row + 16 * ks + 8 + qc);
+      qa[ks][3] = *reinterpret_cast<const uint32_t*>(qb_row + 16 * ks + 8 + qc);
+    }
+  }
+  float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;
+  float o[16][4];  // O [16 rows x 128 dims]: n-tile j = dims 8j .. 8j+7
+#pragma unroll
+  for (int j = 0; j < 16; ++j)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) o[j][e] = 0.f;
+  const int mi = lane >> 3, mr = lane & 7;
+  bool ok = true;
+  int done = 0;
+  for (int kb = 0; kb < nkb; ++kb) {
+    ok = mbar_wait(&bars[kb % APF_NBUF], (uint32_t)((kb / APF_NBUF) & 1), 310);
+    if (!__syncthreads_and(ok)) {
+      ok = false;
+      break;
+    }
+    const uint32_t kbase = smem_u32(smem_apf + (size_t)(kb % APF_NBUF) * 2 * APF_KV_BYTES);
+    const uint32_t vbase = kbase + APF_KV_BYTES;
+    const int k0 = kb * APF_KB;
+    // S [16 rows x 64 keys]: 8 n-tiles of 8 keys
+    float s[8][4];
+#pragma unroll
+    for (int n = 0; n < 8; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) s[n][e] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+#pragma unroll
+      for (int np = 0; np < 4; ++np) {  // pairs of n-tiles: keys 16 np .. 16 np + 15
+        const int key = np * 16 + (mi >> 1) * 8 + mr;
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(kbase + att_swz(key, 2 * ks + (mi & 1)), b0, b1, b2, b3);
+        mma_bf16_16816_full(s[2 * np], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], b0, b1);
+        mma_bf16_16816_full(s[2 * np + 1], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], b2, b3);
+      }
+    }
+    // mask, scale, online softmax for rows row_a (e 0, 1) and row_b (e 2, 3)
+    float mxa = -INFINITY, mxb = -INFINITY;
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
+      const int kk = k0 + 8 * n + qc;
+      s[n][0] = (kk <= row_a && kk < p.P) ? s[n][0] * p.scale : -INFINITY;
+      s[n][1] = (kk + 1 <= row_a && kk + 1 < p.P) ? s[n][1] * p.scale : -INFINITY;
+      s[n][2] = (kk <= row_b && kk < p.P) ? s[n][2] * p.scale : -INFINITY;
+      s[n][3] = (kk + 1 <= row_b && kk + 1 < p.P) ? s[n][3] * p.scale : -INFINITY;
+      mxa = fmaxf(mxa, fmaxf(s[n][0], s[n][1]));
+      mxb = fmaxf(mxb, fmaxf(s[n][2], s[n][3]));
+    }
+    mxa = fmaxf(mxa, __shfl_xor_sync(0xffffffffu, mxa, 1));
+    mxa = fmaxf(mxa, __shfl_xor_sync(0xffffffffu, mxa, 2));
+    mxb = fmaxf(mxb, __shfl_xor_sync(0xffffffffu, mxb, 1));
+    mxb = fmaxf(mxb, __shfl_xor_sync(0xffffffffu, mxb, 2));
+    const float mna = fmaxf(m_a, mxa), mnb = fmaxf(m_b, mxb);
+    // a row whose keys are all masked so far keeps max -inf: use 0 as the reference
+    const float ra = mna == -INFINITY ? 0.f : mna, rb = mnb == -INFINITY ? 0.f : mnb;
+    const float ca = expf(m_a - ra), cb = expf(m_b - rb);
+    float sa = 0.f, sb = 0.f;
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
+      s[n][0] = expf(s[n][0] - ra);
+      s[n][1] = expf(s[n][1] - ra);
+      s[n][2] = expf(s[n][2] - rb);
+      s[n][3] = expf(s[n][3] - rb);
+      sa += s[n][0] + s[n][1];
+      sb += s[n][2] + s[n][3];
+    }
+    sa += __shfl_xor_sync(0xffffffffu, sa, 1);
+    sa += __shfl_xor_sync(0xffffffffu, sa, 2);
+    sb += __shfl_xor_sync(0xffffffffu, sb, 1);
+    sb += __shfl_xor_sync(0xffffffffu, sb, 2);
+    l_a = l_a * ca + sa;
+    l_b = l_b * cb + sb;
+    m_a = mna;
+    m_b = mnb;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      o[j][0] *= ca;
+      o[j][1] *= ca;
+      o[j][2] *= cb;
+      o[j][3] *= cb;
+    }
+    // O += P V: P (A operand, rows = queries, k = keys) from the S fragments as
+    // bf16 hi + lo; V via ldmatrix.trans.  k-step kt = keys 16 kt .. 16 kt + 15.
+#pragma unroll
+    for (int kt = 0; kt < 4; ++kt) {
+      float ph[8], pl[8];
+      const float src8[8] = {s[2 * kt][0], s[2 * kt][1], s[2 * kt][2], s[2 * kt][3],
+                             s[2 * kt + 1][0], s[2 * kt + 1][1], s[2 * kt + 1][2], s[2 * kt + 1][3]};
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        ph[e] = round_bf16(src8[e]);
+        pl[e] = src8[e] - ph[e];
+      }
+      // a0: (row a, keys 16kt + qc..), a1: (row b, same), a2: (row a, keys + 8), a3: (row b, keys + 8)
+      const uint32_t ha0 = pack_bf16x2(ph[0], ph[1]), ha1 = pack_bf16x2(ph[2], ph[3]);
+      const uint32_t ha2 = pack_bf16x2(ph[4], ph[5]), ha3 = pack_bf16x2(ph[6], ph[7]);
+      const uint32_t la0 = pack_bf16x2(pl[0], pl[1]), la1 = pack_bf16x2(pl[2], pl[3]);
+      const uint32_t la2 = pack_bf16x2(pl[4], pl[5]), la3 = pack_bf16x2(pl[6], pl[7]);
+#pragma unroll
+      for (int jj = 0; jj < 8; ++jj) {  // pairs of dim tiles: dims 16 jj .. 16 jj + 15
+        // transposed matrices: (keys 16kt..+7, chunk 2jj), (keys 16kt+8..+15, 2jj), (keys 16kt..+7, 2jj+1), (.., 2jj+1)
+        const int key = kt * 16 + (mi & 1) * 8 + mr;
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_t(vbase + att_swz(key, 2 * jj + (mi >> 1)), b0, b1, b2, b3);
+        mma_bf16_16816_full(o[2 * jj], ha0, ha1, ha2, ha3, b0, b1);
+        mma_bf16_16816_full(o[2 * jj], la0, la1, la2, la3, b0, b1);
+        mma_bf16_16816_full(o[2 * jj + 1], ha0, ha1, ha2, ha3, b2, b3);
+        mma_bf16_16816_full(o[2 * jj + 1], la0, la1, la2, la3, b2, b3);
+      }
+    }
+    __syncthreads();  // every warp is done with the buffer before it is refilled
+    done = kb + 1;
+    if (kb + APF_NBUF < nkb) issue(kb + APF_NBUF);
+  }
+  for (int kb = done; kb < min(nkb, done + APF_NBUF); ++kb) mbar_wait(&bars[kb % APF_NBUF], (uint32_t)((kb / APF_NBUF) & 1), 311);
+  if (!ok) return;
+  // normalise and write rows row_a / row_b, dims 8 j + qc, + 1
+  const float ia = l_a > 0.f ? 1.f / l_a : 0.f, ib = l_b > 0.f ? 1.f / l_b : 0.f;
+  uint16_t* oa = p.out + ((size_t)b * p.P + row_a) * (size_t)(p.n_heads * ATT_D) + h * ATT_D;
+  uint16_t* ob = p.out + ((size_t)b * p.P + row_b) * (size_t)(p.n_heads * ATT_D) + h * ATT_D;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    if (row_a < p.P)
+      *reinterpret_cast<uint32_t*>(oa + 8 * j + qc) = pack_bf16x2(o[j][0] * ia, o[j][1] * ia);
+    if (row_b < p.P)
+      *reinterpret_cast<uint32_t*>(ob + 8 * j + qc) = pack_bf16x2(o[j][2] * ib, o[j][3] * ib);
+  }
+}
+
+}  // namespace bitnet

@@ -18,6 +18,7 @@
 
 #include "act_quant.cuh"
 #include "attention.cuh"
+#include "attention_prefill.cuh"
 #include "bitlinear_simt.cuh"
 #include "bitlinear_tc.cuh"
 #include "common.cuh"
@@ -156,7 +157,8 @@ int to_dev_segments(const bitnet_segments_t* s, int N, int epilogue, bitnet_segm
   return s->end[s->count - 1] == N ? BITNET_OK : BITNET_ERR_INVALID_ARGUMENT;
 }
 
-std::atomic<unsigned long long> g_smem_aq{0}, g_smem_simt[3][4], g_smem_tc[3], g_smem_lmh{0}, g_smem_att[4];
+std::atomic<unsigned long long> g_smem_aq{0}, g_smem_simt[3][4], g_smem_tc[3], g_smem_lmh{0}, g_smem_att[4],
+    g_smem_apf{0};
 
 int lm_head_tile_T(int B) { return round_up(B, 16); }
 size_t lm_head_part_bytes(int B, int grid) { return (size_t)grid * B * sizeof(ArgPair); }
@@ -494,6 +496,59 @@ int bitnet_gqa_decode_attention(const void* qkv, int B, int n_heads, int n_kv_he
       return launch(gqa_decode_kernel<8>, grid, block, smem, stream, 1, p);
     default: return BITNET_ERR_INVALID_ARGUMENT;
   }
+}
+
+int bitnet_rope_append_prefill(const void* qkv, int B, int P, int n_heads, int n_kv_heads, int head_dim,
+                               const void* rope_cos, const void* rope_sin, int rope_len, void* q_out, void* k_cache,
+                               void* v_cache, int max_len, bitnet_stream_t stream) {
+  DevInfo* d;
+  if (int e = device_info(&d)) return e;
+  if (!qkv || !rope_cos || !rope_sin || !q_out || !k_cache || !v_cache) return BITNET_ERR_INVALID_ARGUMENT;
+  if (B <= 0 || P <= 0 || n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads != 0 || head_dim != ATT_D ||
+      P > max_len || P > rope_len)
+    return BITNET_ERR_INVALID_ARGUMENT;
+  if (!aligned(qkv, 2) || !aligned(q_out, 2) || !aligned(k_cache, 2) || !aligned(v_cache, 2)) return BITNET_ERR_ALIGNMENT;
+  RopePrefillParams p;
+  p.qkv = (const uint16_t*)qkv;
+  p.B = B;
+  p.P = P;
+  p.n_heads = n_heads;
+  p.n_kv = n_kv_heads;
+  p.rope_cos = (const uint16_t*)rope_cos;
+  p.rope_sin = (const uint16_t*)rope_sin;
+  p.q_out = (uint16_t*)q_out;
+  p.k_cache = (uint16_t*)k_cache;
+  p.v_cache = (uint16_t*)v_cache;
+  p.max_len = max_len;
+  const size_t total = (size_t)B * P * (n_heads + n_kv_heads) * 64;
+  const int grid = (int)std::min<size_t>((total + 255) / 256, (size_t)d->sms * 16);
+  return launch(rope_append_prefill_kernel, dim3(grid), dim3(256), 0, stream, 1, p);
+}
+
+int bitnet_attention_prefill(const void* q, const void* k_cache, const void* v_cache, int B, int P, int n_heads,
+                             int n_kv_heads, int head_dim, int max_len, float scale, void* out,
+                             bitnet_stream_t stream) {
+  DevInfo* d;
+  if (int e = device_info(&d)) return e;
+  if (!q || !k_cache || !v_cache || !out) return BITNET_ERR_INVALID_ARGUMENT;
+  if (B <= 0 || P <= 0 || n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads != 0 || head_dim != ATT_D ||
+      P > max_len)
+    return BITNET_ERR_INVALID_ARGUMENT;
+  if (!aligned(q, 4) || !aligned(out, 4) || !aligned(k_cache, 16) || !aligned(v_cache, 16)) return BITNET_ERR_ALIGNMENT;
+  if (int e = ensure_smem(attention_prefill_kernel, &g_smem_apf)) return e;
+  AttnPrefillParams p;
+  p.q = (const uint16_t*)q;
+  p.k_cache = (const uint16_t*)k_cache;
+  p.v_cache = (const uint16_t*)v_cache;
+  p.B = B;
+  p.P = P;
+  p.n_heads = n_heads;
+  p.n_kv = n_kv_heads;
+  p.max_len = max_len;
+  p.scale = scale;
+  p.out = (uint16_t*)out;
+  return launch(attention_prefill_kernel, dim3((P + APF_QB - 1) / APF_QB, n_heads, B), dim3(APF_THREADS), APF_SMEM,
+                stream, 1, p);
 }
 
 size_t bitnet_lm_head_bytes(int V, int K) {

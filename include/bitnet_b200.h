@@ -233,6 +233,22 @@ int bitnet_decode_plan_create(const bitnet_decode_desc_t* desc, bitnet_decode_pl
 int bitnet_decode_plan_run(bitnet_decode_plan_t* plan, bitnet_stream_t stream);
 int bitnet_decode_plan_destroy(bitnet_decode_plan_t* plan);
 
+/* ---- prefill (prompt) attention ------------------------------------------
+ * Replaces the prefill branch of the attention (src/bitnet_tt/layers/
+ * attention.py:1348-1507 and model/bitnet.py:217-313: all prompt tokens of a
+ * batch in one pass).
+ * bitnet_rope_append_prefill: qkv bf16 [B*P, (n_heads + 2 n_kv) * 128] (token
+ * b*P + p at position p) -> rotated queries q_out bf16 [B*P, n_heads * 128];
+ * rotated keys and the values written to cache rows 0 .. P-1.
+ * bitnet_attention_prefill: causal GQA attention of every prompt token over
+ * the cache rows 0 .. its position; out bf16 [B*P, n_heads * 128]. */
+int bitnet_rope_append_prefill(const void* qkv, int B, int P, int n_heads, int n_kv_heads, int head_dim,
+                               const void* rope_cos, const void* rope_sin, int rope_len, void* q_out, void* k_cache,
+                               void* v_cache, int max_len, bitnet_stream_t stream);
+int bitnet_attention_prefill(const void* q, const void* k_cache, const void* v_cache, int B, int P, int n_heads,
+                             int n_kv_heads, int head_dim, int max_len, float scale, void* out,
+                             bitnet_stream_t stream);
+
 /* ---- lm_head / embedding table -------------------------------------------
  * The tied embedding / lm_head matrix (src/bitnet_tt/utils/weights.py:236-246)
  * is stored once, in a tiled layout read by both the lm_head and the gather. */

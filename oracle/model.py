@@ -165,6 +165,49 @@ class OracleBitNet:
             out[i] = torch.einsum("hgl,hld->hgd", pr, vals).reshape(nq, d)
         return bf(out.reshape(b, nq * d))
 
+    def prefill_attention(self, qkv: torch.Tensor, b: int, plen: int, cache) -> torch.Tensor:
+        """Causal attention of b prompts of plen tokens at positions 0 .. plen-1
+        (qkv [b*plen, (nq + 2 nkv) d]): the reference's prefill branch
+        (src/bitnet_tt/layers/attention.py:1348-1507: RoPE over the prompt 1396,
+        fill_cache_range 1411-1418, causal SDPA with scale d^-0.5 1465-1484).
+        Writes cache rows 0 .. plen-1; returns bf16-valued [b*plen, nq d]."""
+        d, nq, nkv = self.d, self.nq, self.nkv
+        x = qkv.reshape(b, plen, -1)
+        q = x[..., : nq * d].reshape(b, plen, nq, d)
+        k = x[..., nq * d:(nq + nkv) * d].reshape(b, plen, nkv, d)
+        v = x[..., (nq + nkv) * d:].reshape(b, plen, nkv, d)
+        cos, sin = self.cos[:plen][None, :, None, :], self.sin[:plen][None, :, None, :]
+        q, k = rope(q, cos, sin), rope(k, cos, sin)
+        kc, vc = cache
+        kc[:, :, :plen] = k.permute(0, 2, 1, 3)
+        vc[:, :, :plen] = v.permute(0, 2, 1, 3)
+        g = nq // nkv
+        qh = q.permute(0, 2, 1, 3).reshape(b, nkv, g, plen, d)
+        sc = torch.einsum("bhgpd,bhld->bhgpl", qh, kc[:, :, :plen]) * (d ** -0.5)
+        causal = torch.ones(plen, plen, dtype=torch.bool).triu(1)
+        sc = sc.masked_fill(causal, float("-inf"))
+        o = torch.einsum("bhgpl,bhld->bhgpd", torch.softmax(sc, dim=-1), vc[:, :, :plen])
+        return bf(o.reshape(b, nq, plen, d).permute(0, 2, 1, 3).reshape(b * plen, nq * d))
+
+    def prefill(self, prompts: np.ndarray, caches) -> tuple[torch.Tensor, torch.Tensor]:
+        """All prompt tokens [B, L] in one batched pass (src/bitnet_tt/model/
+        bitnet.py:217-313, mode "prefill"); fills cache rows 0 .. L-1 and returns
+        (first generated ids [B], bf16-valued logits of the last prompt tokens)."""
+        b, plen = prompts.shape
+        h = self.embed[torch.from_numpy(prompts.reshape(-1).astype(np.int64))]
+        for L, cache in zip(self.layers, caches):
+            qkv = bitlinear(h, L.in_ln, self.eps, L.w_qkv, L.s_qkv)
+            a = self.prefill_attention(qkv, b, plen, cache)
+            h = bf(h + bitlinear(a, L.attn_ln, self.eps, L.w_o, L.s_o))
+            n = rmsnorm(h, L.post_ln, self.eps)
+            g = bitlinear(n, None, self.eps, L.w_g, L.s_g)
+            u = bitlinear(n, None, self.eps, L.w_u, L.s_u)
+            mid = bf(torch.where(g > 0, bf(g * g), torch.zeros_like(g)) * u)
+            h = bf(h + bitlinear(mid, L.ffn_ln, self.eps, L.w_d, L.s_d))
+        last = h.reshape(b, plen, -1)[:, -1]
+        logits = bf(rmsnorm(last, self.norm, self.eps) @ self.lm_head.t())
+        return torch.argmax(logits, dim=-1).to(torch.int32), logits
+
     def step(self, ids: torch.Tensor, pos: torch.Tensor, caches) -> tuple[torch.Tensor, torch.Tensor]:
         """One greedy decode step: (next ids [B], bf16-valued logits [B, V])."""
         h = self.embed[ids.long()]

@@ -138,3 +138,30 @@ def test_oracle_model_small_decode_runs():
     toks, logits = o.generate(prompts, 3)
     assert toks.shape == (3, 3) and len(logits) == 3
     assert toks.min() >= 0 and toks.max() < 300
+
+
+def test_oracle_batched_prefill_equals_token_by_token():
+    """The oracle's batched prefill (causal attention over the prompt) equals
+    the prompt run through its decode step one token at a time: same caches,
+    same last-token logits, same first ids (the orders of its fp32 sums do not
+    reach the bf16 results on this case)."""
+    import torch
+
+    from bitnet_tt.config import BitNetConfig
+    from bitnet_tt.utils.weights import synthetic_state_dict
+
+    cfg = BitNetConfig(hidden_size=256, num_layers=2, num_attention_heads=4, num_key_value_heads=2,
+                       intermediate_size=512, vocab_size=300)
+    o = om.OracleBitNet(cfg, synthetic_state_dict(cfg, 4), max_len=32)
+    prompts = np.random.default_rng(2).integers(0, 300, size=(3, 9))
+    caches = o.new_cache(3)
+    ids, logits = o.prefill(prompts, caches)
+    step_caches = o.new_cache(3)
+    pos = torch.zeros(3, dtype=torch.int32)
+    for t in range(prompts.shape[1]):
+        nxt, step_logits = o.step(torch.from_numpy(prompts[:, t].astype(np.int32)), pos, step_caches)
+        pos = pos + 1
+    assert torch.equal(ids, nxt)
+    assert torch.allclose(logits, step_logits, rtol=1e-2, atol=1e-2)
+    for (k, v), (ks, vs) in zip(caches, step_caches):
+        assert torch.allclose(k, ks, rtol=1e-2, atol=1e-2) and torch.allclose(v, vs, rtol=1e-2, atol=1e-2)

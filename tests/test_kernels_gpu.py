@@ -182,6 +182,15 @@ def test_bitlinear_tcgen05_decode_shapes(cuda, m, n, k, epilogue, split):
     check_bitlinear(cuda, m, n, k, path=2, epilogue=epilogue, seed=n + k, split=split)
 
 
+@pytest.mark.parametrize("m,n,k,epilogue", [
+    (1000, 3840, 2560, "none"),           # prefill token tiles of 256, ragged last tile
+    (4096, 2560, 6912, "residual_add"),   # down shape over 16 token tiles
+    (2048, 1024, 2560, "relu2_mul"),
+])
+def test_bitlinear_tcgen05_prefill_shapes(cuda, m, n, k, epilogue):
+    check_bitlinear(cuda, m, n, k, path=2, epilogue=epilogue, seed=m + n)
+
+
 @pytest.mark.parametrize("path", [1, 2])
 def test_bitlinear_config0_full_size(cuda, path):
     """x [32, 2560], W [6912, 2560] with P(0) = 0.4, scale 0.02."""

@@ -119,6 +119,144 @@ def test_attention_position_beyond_max_ctx_is_a_device_error(cuda):
         _lib.gqa_decode_attention(qkv, nh, nkv, d, pos, cos.to(cuda), sin.to(cuda), kd, vd, 1.0, out, 512, None)
 
 
+def _prefill_attention_case(cuda, b, plen, nh, nkv, max_len, seed=5):
+    from bitnet_tt import _lib
+    from bitnet_tt.utils.rope import half_split_tables
+
+    d = 128
+    g = torch.Generator().manual_seed(seed)
+    qkv = torch.randn((b * plen, (nh + 2 * nkv) * d), generator=g).to(torch.bfloat16)
+    kc = torch.randn((b, nkv, max_len, d), generator=g).to(torch.bfloat16)
+    vc = torch.randn((b, nkv, max_len, d), generator=g).to(torch.bfloat16)
+    cos, sin = half_split_tables(d, max_len, 500000.0)
+    kd, vd = kc.to(cuda), vc.to(cuda)
+    q = torch.empty((b * plen, nh * d), dtype=torch.bfloat16, device=cuda)
+    out = torch.empty((b * plen, nh * d), dtype=torch.bfloat16, device=cuda)
+    _lib.rope_append_prefill(qkv.to(cuda), b, plen, nh, nkv, cos.to(cuda), sin.to(cuda), q, kd, vd)
+    _lib.attention_prefill(q, kd, vd, b, plen, nh, nkv, d ** -0.5, out)
+    torch.cuda.synchronize()
+    assert _lib.last_device_status()[0] == 0
+
+    o = om.OracleBitNet.__new__(om.OracleBitNet)
+    o.d, o.nq, o.nkv = d, nh, nkv
+    o.cos, o.sin = om.rope_tables(d, max_len, 500000.0)
+    cache = (kc.float().clone(), vc.float().clone())
+    ref = o.prefill_attention(qkv.float(), b, plen, cache)
+    # cache rows 0 .. plen-1 written bit-exactly (RoPE in bf16 ops, V copied), the rest untouched
+    assert torch.equal(kd.float().cpu(), cache[0])
+    assert torch.equal(vd.float().cpu(), cache[1])
+    qr = om.rope(qkv.float()[:, : nh * d].reshape(b, plen, nh, d), o.cos[:plen][None, :, None], o.sin[:plen][None, :, None])
+    assert torch.equal(q.float().cpu(), qr.reshape(b * plen, nh * d))
+    np.testing.assert_allclose(out.float().cpu().numpy(), ref.numpy(), rtol=2e-2, atol=2e-2)
+
+
+@pytest.mark.parametrize("b,plen,nh,nkv,max_len", [
+    (2, 150, 4, 2, 160),    # ragged last query / key block
+    (1, 64, 8, 1, 64),      # group of 8 query heads, cache exactly the prompt
+    (3, 1, 4, 4, 8),        # one-token prompts
+    (1, 300, 20, 5, 512),   # BitNet-2B heads
+    (2, 513, 2, 1, 600),    # key blocks past 8
+])
+def test_attention_prefill_matches_oracle(cuda, b, plen, nh, nkv, max_len):
+    _prefill_attention_case(cuda, b, plen, nh, nkv, max_len, seed=b * 1000 + plen)
+
+
+def test_attention_prefill_rejects_bad_arguments(cuda):
+    from bitnet_tt import _lib
+
+    kc = torch.zeros((1, 1, 16, 128), dtype=torch.bfloat16, device=cuda)
+    q = torch.zeros((32, 256), dtype=torch.bfloat16, device=cuda)
+    with pytest.raises(RuntimeError, match="invalid argument"):
+        _lib.attention_prefill(q, kc, kc, 1, 32, 2, 1, 0.1, q)  # prompt longer than the cache
+    with pytest.raises(RuntimeError, match="invalid argument"):
+        _lib.attention_prefill(q, kc, kc, 2, 16, 3, 2, 0.1, q)  # heads not a multiple of kv heads
+
+
+@pytest.mark.parametrize("batch,plen", [(4, 70), (32, 8)])
+def test_batched_prefill_matches_oracle(cuda, batch, plen):
+    """Generator prefill (all prompt tokens per kernel) against the oracle's
+    batched prefill: first ids, logits of the last prompt tokens, KV caches."""
+    from bitnet_tt.inference import Batch32Generator
+
+    cfg = _small_cfg()
+    sd = _numpy_sd(cfg, seed=21)
+    model = _device_model(cfg, sd, cuda)
+    prompts = np.random.default_rng(batch * plen).integers(0, cfg.vocab_size, size=(batch, plen))
+    gen = Batch32Generator(model, batch_size=batch, max_seq_len=128, keep_logits=True)
+    gen.prefill(prompts)
+    assert gen.state.positions.cpu().tolist() == [plen] * batch
+    dev_ids, dev_logits = gen.state.ids.cpu().numpy(), gen.state.logits.float().cpu()
+    oracle = om.OracleBitNet(cfg, sd, max_len=128)
+    caches = oracle.new_cache(batch)
+    ref_ids, ref_logits = oracle.prefill(prompts, caches)
+    rel = (dev_logits - ref_logits).norm() / ref_logits.norm()
+    assert rel < 2e-2, f"logits rel err {rel:.3e}"
+    assert not np.any((dev_ids != ref_ids.numpy()) & ~_near_tie(ref_logits).numpy())
+    # layer 0 sees identical inputs: its keys and values are bit-exact
+    c0 = gen.state.caches[0]
+    assert torch.equal(c0.key_cache[:, :, :plen].float().cpu(), caches[0][0][:, :, :plen])
+    assert torch.equal(c0.value_cache[:, :, :plen].float().cpu(), caches[0][1][:, :, :plen])
+    for c, (kr, vr) in zip(gen.state.caches, caches):
+        for dev, ref in ((c.key_cache, kr), (c.value_cache, vr)):
+            d = dev[:, :, :plen].float().cpu()
+            assert (d - ref[:, :, :plen]).norm() / ref[:, :, :plen].norm() < 2e-2
+
+
+def test_ragged_prompts_batched_prefill_equals_decode_prefill(cuda):
+    """Ragged prompts: the shortest length in one batched pass, the rest by the
+    decode graph -- against every prompt token through the decode graph."""
+    from bitnet_tt.inference import Batch32Generator
+
+    cfg = _small_cfg()
+    sd = _numpy_sd(cfg, seed=5)
+    model = _device_model(cfg, sd, cuda)
+    rng = np.random.default_rng(3)
+    lens = [5, 12, 9, 5, 17, 6, 5, 8]
+    prompts = [rng.integers(0, cfg.vocab_size, size=n) for n in lens]
+    runs = []
+    for batched in (True, False):
+        gen = Batch32Generator(model, batch_size=len(lens), max_seq_len=64, keep_logits=True)
+        gen.batched_prefill = batched
+        gen.prefill(prompts)
+        ids, logits = [gen.state.ids.cpu().numpy().copy()], [gen.state.logits.float().cpu().clone()]
+        for _ in range(4):
+            gen.step()
+            ids.append(gen.state.ids.cpu().numpy().copy())
+            logits.append(gen.state.logits.float().cpu().clone())
+        # every sequence steps with the batch: the shorter ones generate while the longer finish their prompts
+        assert gen.state.positions.cpu().tolist() == [max(lens) + 4] * len(lens)
+        runs.append((np.stack(ids, 1), logits))
+    (ta, la), (tb, lb) = runs
+    rel = (la[0] - lb[0]).norm() / lb[0].norm()
+    assert rel < 2e-2, f"logits rel err {rel:.3e}"
+    for b in range(len(lens)):
+        for t in range(ta.shape[1]):
+            if ta[b, t] != tb[b, t]:
+                assert bool(_near_tie(lb[t][b:b + 1])[0]), f"seq {b} step {t}: not a near-tie"
+                break
+
+
+def test_full_width_prefill_matches_oracle(cuda):
+    """2B-4T widths, 2 layers, 4 prompts of 512 tokens (2048 prompt tokens:
+    8 BitLinear token tiles, 8 key blocks per sequence)."""
+    from bitnet_tt.config import BitNet2B4TConfig
+    from bitnet_tt.inference import Batch32Generator
+
+    cfg = BitNet2B4TConfig(num_layers=2, max_position_embeddings=1024)
+    sd = _numpy_sd(cfg, seed=77)
+    model = _device_model(cfg, sd, cuda)
+    prompts = np.random.default_rng(9).integers(0, cfg.vocab_size, size=(4, 512))
+    gen = Batch32Generator(model, batch_size=4, max_seq_len=576, keep_logits=True)
+    gen.prefill(prompts)
+    dev_logits = gen.state.logits.float().cpu()
+    oracle = om.OracleBitNet(cfg, sd, max_len=576)
+    ref_ids, ref_logits = oracle.prefill(prompts, oracle.new_cache(4))
+    rel = (dev_logits - ref_logits).norm() / ref_logits.norm()
+    assert rel < 2e-2, f"logits rel err {rel:.3e}"
+    mismatch = gen.state.ids.cpu().numpy() != ref_ids.numpy()
+    assert not np.any(mismatch & ~_near_tie(ref_logits).numpy())
+
+
 def test_lm_head_argmax_and_embedding(cuda):
     from bitnet_tt import _lib
 
