@@ -107,6 +107,9 @@ def parse() -> argparse.Namespace:
     p.add_argument("--ref-budget-s", type=float, default=60.0, help="timed CPU work of --impl reference")
     p.add_argument("--prefill-len", type=int, default=512,
                    help="config 3: time a batched prefill of --batch prompts of this length (0: skip)")
+    p.add_argument("--prefill-only", action="store_true",
+                   help="print only the config-3 prefill measurement (one GPU; for launch lists and captures)")
+    p.add_argument("--prefill-reps", type=int, default=3)
     p.add_argument("--decode-path", choices=["per-op", "persistent"], default="per-op",
                    help="per-op: 9 launches per layer; persistent: every layer in one launch")
     p.add_argument("--vocab-shard", action="store_true",
@@ -444,6 +447,19 @@ def prefill_measure(model, args, device, reps: int = 3) -> dict:
     }
 
 
+def run_prefill_only(args) -> None:
+    from bitnet_tt.model import create_model
+    from bitnet_tt.utils.weights import load_weights_to_model, synthetic_state_dict
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    cfg = model_config(args)
+    model = create_model(cfg, device)
+    load_weights_to_model(model, synthetic_state_dict(cfg, args.seed, device=device))
+    torch.cuda.synchronize(device)
+    print(json.dumps({"prefill": prefill_measure(model, args, device, reps=args.prefill_reps)}), flush=True)
+
+
 def run_b200(args) -> None:
     world, rank, local = dist_setup(args)
     device = torch.device("cuda", local)
@@ -611,6 +627,8 @@ def main() -> None:
         raise SystemExit("--warmup must be >= 3")
     if args.impl == "reference":
         run_reference(args)
+    elif args.prefill_only:
+        run_prefill_only(args)
     else:
         run_b200(args)
 

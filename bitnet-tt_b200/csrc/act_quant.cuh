@@ -275,4 +275,182 @@ act_quant_vec_kernel(const uint16_t* __restrict__ x, int M, int K, int ldx, cons
                 threadIdx.x);
 }
 
+// Many-row path (prefill): one warp per token row, 8 rows per CTA, every
+// reduction a warp shuffle (no block barrier).  Lane l keeps chunks
+// l, l + 32, ... (up to MAXC of 8 elements) in registers.  Same results as
+// aq_row_vec: fp64 sum of squares (exact in any order), max, integer sum.
+// The 8 rows of a CTA share each 128-byte core matrix of the tiled code
+// layout, so the CTA writes whole lines.  Requirements as for
+// act_quant_vec_kernel, and Kp <= 8 * 32 * MAXC.
+template <int MAXC>
+__global__ void __launch_bounds__(256)
+act_quant_warp_kernel(const uint16_t* __restrict__ x, int M, int K, int ldx, const uint16_t* __restrict__ gamma,
+                      float eps, int8_t* __restrict__ q, float* __restrict__ row_scale, int32_t* __restrict__ row_sum,
+                      uint16_t* __restrict__ normed_out, int T, int Kp) {
+  pdl_trigger();
+  const int lane = threadIdx.x & 31;
+  const int m = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const bool valid = m < M;
+  const int KC8 = K >> 3;
+  pdl_wait();
+  uint4 xr[MAXC];
+#pragma unroll
+  for (int c = 0; c < MAXC; ++c) {
+    const int ch = lane + 32 * c;
+    xr[c] = (valid && ch < KC8) ? reinterpret_cast<const uint4*>(x + (size_t)m * ldx)[ch] : make_uint4(0, 0, 0, 0);
+  }
+  if (gamma != nullptr) {
+    double ss = 0.0;
+#pragma unroll
+    for (int c = 0; c < MAXC; ++c) {
+      float f[8];
+      aq_unpack8(xr[c], f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss = fma((double)f[e], (double)f[e], ss);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float var = __double2float_rn(__ddiv_rn(ss, (double)K));
+    const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+#pragma unroll
+    for (int c = 0; c < MAXC; ++c) {
+      // gamma is read here, not kept in registers: every row of the launch
+      // reads the same few KB, which stay in L1
+      const int ch = lane + 32 * c;
+      const uint4 gv = ch < KC8 ? reinterpret_cast<const uint4*>(gamma)[ch] : make_uint4(0, 0, 0, 0);
+      float f[8], g[8];
+      aq_unpack8(xr[c], f);
+      aq_unpack8(gv, g);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) f[e] = round_bf16(__fmul_rn(g[e], round_bf16(__fmul_rn(f[e], r))));
+      xr[c] = aq_pack8(f);
+    }
+  }
+  if (normed_out != nullptr && valid) {
+#pragma unroll
+    for (int c = 0; c < MAXC; ++c) {
+      const int ch = lane + 32 * c;
+      if (ch < KC8) reinterpret_cast<uint4*>(normed_out + (size_t)m * K)[ch] = xr[c];
+    }
+  }
+  if (q == nullptr) return;
+  float amax = 0.f;
+#pragma unroll
+  for (int c = 0; c < MAXC; ++c) {
+    float f[8];
+    aq_unpack8(xr[c], f);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(f[e]));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  amax = fmaxf(amax, 1e-5f);
+  const float s = __fdiv_rn(127.0f, amax);
+  int qsum = 0;
+#pragma unroll
+  for (int c = 0; c < MAXC; ++c) {
+    const int ch = lane + 32 * c;
+    if (ch * 8 < Kp) {  // chunks past K (up to Kp) are written as zeros
+      float f[8];
+      aq_unpack8(xr[c], f);
+      uint32_t lo = 0, hi = 0;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        int qi = 0;
+        if (valid && ch < KC8) qi = max(-128, min(127, __float2int_rn(__fmul_rn(f[e], s))));
+        qsum += qi;
+        if (e < 4)
+          lo |= ((uint32_t)(qi & 0xFF)) << (8 * e);
+        else
+          hi |= ((uint32_t)(qi & 0xFF)) << (8 * (e - 4));
+      }
+      *reinterpret_cast<uint2*>(q + alayout_offset(m, ch * 8, T, Kp)) = make_uint2(lo, hi);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) qsum += __shfl_xor_sync(0xffffffffu, qsum, o);
+  if (lane == 0) {
+    row_scale[m] = valid ? s : 1.0f;
+    row_sum[m] = qsum;
+  }
+}
+
+// Many-row path for long rows (K > 2560, the FFN width): one warp per row as
+// above, but the row is not held in registers; it is read three times (sum of
+// squares, absmax of the normalised values, codes).  A CTA's 8 rows (at most
+// 8 x 16 KB) stay in L1 between the passes, so DRAM reads the row once.
+__global__ void __launch_bounds__(256)
+act_quant_warp_stream_kernel(const uint16_t* __restrict__ x, int M, int K, int ldx, const uint16_t* __restrict__ gamma,
+                             float eps, int8_t* __restrict__ q, float* __restrict__ row_scale,
+                             int32_t* __restrict__ row_sum, uint16_t* __restrict__ normed_out, int T, int Kp) {
+  pdl_trigger();
+  pdl_wait();
+  const int lane = threadIdx.x & 31;
+  const int m = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const bool valid = m < M;
+  const int KC8 = K >> 3, KP8 = Kp >> 3;
+  const uint4* xrow = reinterpret_cast<const uint4*>(x + (size_t)m * ldx);
+  const uint4* grow = reinterpret_cast<const uint4*>(gamma);
+  float r = 1.f;
+  if (gamma != nullptr) {
+    double ss = 0.0;
+    for (int ch = lane; ch < KC8; ch += 32) {
+      float f[8];
+      aq_unpack8(valid ? xrow[ch] : make_uint4(0, 0, 0, 0), f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss = fma((double)f[e], (double)f[e], ss);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float var = __double2float_rn(__ddiv_rn(ss, (double)K));
+    r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+  }
+  // normalised chunk ch (packed bf16) -> f
+  auto chunk = [&](int ch, float* f) {
+    aq_unpack8((valid && ch < KC8) ? xrow[ch] : make_uint4(0, 0, 0, 0), f);
+    if (gamma != nullptr) {
+      float g[8];
+      aq_unpack8(ch < KC8 ? grow[ch] : make_uint4(0, 0, 0, 0), g);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) f[e] = round_bf16(__fmul_rn(g[e], round_bf16(__fmul_rn(f[e], r))));
+    }
+  };
+  float amax = 0.f;
+  for (int ch = lane; ch < KC8; ch += 32) {
+    float f[8];
+    chunk(ch, f);
+    if (normed_out != nullptr && valid) reinterpret_cast<uint4*>(normed_out + (size_t)m * K)[ch] = aq_pack8(f);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(f[e]));
+  }
+  if (q == nullptr) return;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  amax = fmaxf(amax, 1e-5f);
+  const float s = __fdiv_rn(127.0f, amax);
+  int qsum = 0;
+  for (int ch = lane; ch < KP8; ch += 32) {  // chunks past K (up to Kp) are written as zeros
+    float f[8];
+    chunk(ch, f);
+    uint32_t lo = 0, hi = 0;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      int qi = 0;
+      if (valid && ch < KC8) qi = max(-128, min(127, __float2int_rn(__fmul_rn(f[e], s))));
+      qsum += qi;
+      if (e < 4)
+        lo |= ((uint32_t)(qi & 0xFF)) << (8 * e);
+      else
+        hi |= ((uint32_t)(qi & 0xFF)) << (8 * (e - 4));
+    }
+    *reinterpret_cast<uint2*>(q + alayout_offset(m, ch * 8, T, Kp)) = make_uint2(lo, hi);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) qsum += __shfl_xor_sync(0xffffffffu, qsum, o);
+  if (lane == 0) {
+    row_scale[m] = valid ? s : 1.0f;
+    row_sum[m] = qsum;
+  }
+}
+
 }  // namespace bitnet

@@ -1,8 +1,8 @@
 // Prefill (prompt) path of the attention: RoPE + KV-cache write for all prompt
 // positions, then causal GQA attention over the prompt.
 //
-// rope_append_prefill_kernel: one thread per (token, head, pair of dims
-// (i, i + 64)); the same bf16 op-by-op half-split RoPE as the decode kernel:
+// rope_append_prefill_kernel: one CTA per token; the same bf16 op-by-op
+// half-split RoPE as the decode kernel:
 //     out[i]    = bf16(bf16(x[i] * cos_i)    + bf16(-x[i+64] * sin_i))
 //     out[i+64] = bf16(bf16(x[i+64] * cos_i) + bf16( x[i]    * sin_i))
 // Rotated queries go to q_out [B*P, n_heads*128]; rotated keys and the values
@@ -38,38 +38,44 @@ struct RopePrefillParams {
   int max_len;
 };
 
+// grid = B * P (one CTA per prompt token), 256 threads; a thread takes dims
+// (d, d + 1) and (d + 64, d + 65) of one head with 4-byte accesses.
 __global__ void __launch_bounds__(256) rope_append_prefill_kernel(const RopePrefillParams p) {
   pdl_trigger();
   pdl_wait();
+  const int tok = blockIdx.x;
+  const int pos = tok % p.P, b = tok / p.P;
   const int nh = p.n_heads + p.n_kv;  // heads that get a rotation
-  const size_t total = (size_t)p.B * p.P * nh * 64;
-  for (size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += (size_t)gridDim.x * blockDim.x) {
-    const int i = (int)(idx % 64);
-    const size_t th = idx / 64;
-    const int hh = (int)(th % nh);
-    const size_t tok = th / nh;
-    const int pos = (int)(tok % p.P);
-    const int b = (int)(tok / p.P);
-    const uint16_t* row = p.qkv + tok * (size_t)((p.n_heads + 2 * p.n_kv) * ATT_D);
-    const uint16_t* src = row + (size_t)hh * ATT_D;
-    const float c = bf16_bits_to_f32(p.rope_cos[(size_t)pos * 64 + i]);
-    const float s = bf16_bits_to_f32(p.rope_sin[(size_t)pos * 64 + i]);
-    const float x1 = bf16_bits_to_f32(src[i]);
-    const float x2 = bf16_bits_to_f32(src[i + 64]);
-    const uint16_t o1 = f32_to_bf16_bits(round_bf16(__fadd_rn(round_bf16(__fmul_rn(x1, c)), round_bf16(__fmul_rn(-x2, s)))));
-    const uint16_t o2 = f32_to_bf16_bits(round_bf16(__fadd_rn(round_bf16(__fmul_rn(x2, c)), round_bf16(__fmul_rn(x1, s)))));
+  const uint16_t* row = p.qkv + (size_t)tok * (size_t)((p.n_heads + 2 * p.n_kv) * ATT_D);
+  const uint32_t* cs = reinterpret_cast<const uint32_t*>(p.rope_cos + (size_t)pos * 64);
+  const uint32_t* sn = reinterpret_cast<const uint32_t*>(p.rope_sin + (size_t)pos * 64);
+  for (int it = threadIdx.x; it < nh * 32; it += blockDim.x) {
+    const int hh = it >> 5, d = (it & 31) * 2;
+    const uint32_t x1 = *reinterpret_cast<const uint32_t*>(row + hh * ATT_D + d);
+    const uint32_t x2 = *reinterpret_cast<const uint32_t*>(row + hh * ATT_D + 64 + d);
+    const uint32_t c2 = cs[d >> 1], s2 = sn[d >> 1];
+    uint32_t o1 = 0, o2 = 0;
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const float a = bf16_bits_to_f32((uint16_t)(x1 >> (16 * e))), bb = bf16_bits_to_f32((uint16_t)(x2 >> (16 * e)));
+      const float c = bf16_bits_to_f32((uint16_t)(c2 >> (16 * e))), sv = bf16_bits_to_f32((uint16_t)(s2 >> (16 * e)));
+      const uint16_t r1 = f32_to_bf16_bits(round_bf16(__fadd_rn(round_bf16(__fmul_rn(a, c)), round_bf16(__fmul_rn(-bb, sv)))));
+      const uint16_t r2 = f32_to_bf16_bits(round_bf16(__fadd_rn(round_bf16(__fmul_rn(bb, c)), round_bf16(__fmul_rn(a, sv)))));
+      o1 |= (uint32_t)r1 << (16 * e);
+      o2 |= (uint32_t)r2 << (16 * e);
+    }
     if (hh < p.n_heads) {
-      uint16_t* dst = p.q_out + tok * (size_t)(p.n_heads * ATT_D) + (size_t)hh * ATT_D;
-      dst[i] = o1;
-      dst[i + 64] = o2;
+      uint16_t* dst = p.q_out + (size_t)tok * (size_t)(p.n_heads * ATT_D) + hh * ATT_D;
+      *reinterpret_cast<uint32_t*>(dst + d) = o1;
+      *reinterpret_cast<uint32_t*>(dst + 64 + d) = o2;
     } else {
       const int g = hh - p.n_heads;
       const size_t crow = (((size_t)b * p.n_kv + g) * p.max_len + pos) * ATT_D;
-      p.k_cache[crow + i] = o1;
-      p.k_cache[crow + i + 64] = o2;
+      *reinterpret_cast<uint32_t*>(p.k_cache + crow + d) = o1;
+      *reinterpret_cast<uint32_t*>(p.k_cache + crow + 64 + d) = o2;
       const uint16_t* vsrc = row + (size_t)(p.n_heads + p.n_kv + g) * ATT_D;
-      p.v_cache[crow + i] = vsrc[i];
-      p.v_cache[crow + i + 64] = vsrc[i + 64];
+      *reinterpret_cast<uint32_t*>(p.v_cache + crow + d) = *reinterpret_cast<const uint32_t*>(vsrc + d);
+      *reinterpret_cast<uint32_t*>(p.v_cache + crow + 64 + d) = *reinterpret_cast<const uint32_t*>(vsrc + 64 + d);
     }
   }
 }

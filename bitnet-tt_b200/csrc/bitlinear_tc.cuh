@@ -28,11 +28,14 @@
 //               ring of shared-memory slots (weights of the first slots before
 //               griddepcontrol.wait, so they overlap the previous kernel), the
 //               tile's per-token scales / row sums into shared memory, refills.
-// Epilogue: the unpacker warps sum D_0..D_{NACC-1} (tcgen05.ld) into shared
-// memory; with a K split (grid z = cluster size > 1) every CTA pushes each
-// token's partials into the CTA of the cluster that owns the token through
-// distributed shared memory, and each owner finishes its tokens.  No global
-// scratch is used.
+// Epilogue without a K split: all 12 warps read D (tcgen05.ld; warp w reads
+// lane quarter w % 4), finish each value to its bf16 result and stage the tile
+// token-major in the idle ring; then they write whole output rows with 16-byte
+// stores (residual read in batches ahead of the stores).  With a K split (grid
+// z = cluster size > 1) the unpacker warps sum D_0..D_{NACC-1} into shared
+// memory, every CTA pushes each token's partials into the CTA of the cluster
+// that owns the token through distributed shared memory, and each owner
+// finishes its tokens.  No global scratch is used.
 #pragma once
 #include "common.cuh"
 #include "epilogue.cuh"
@@ -52,6 +55,7 @@ constexpr int TC_MAX_SLOTS = 16;
 constexpr int TC_MAX_NBUF = 8;      // A buffers in TMEM (64 columns each)
 constexpr int TC_TMEM_COLS = 512;       // one CTA per SM; 256 when two CTAs share an SM
 constexpr int TC_CTRL_BYTES = 5120;
+constexpr int TC_ST_LD = 136;  // bf16 row stride of the staged output tile (272 B: rows stay 16-byte aligned)
 
 struct TcParams {
   const int8_t* q;
@@ -93,13 +97,17 @@ struct TcCtrl {
   uint64_t recv_full;  // split > 1: the peers' partials for this CTA's tokens have landed
   uint32_t tmem_base;
   int abort_flag;
-  float scale[256];  // row_scale of the tile's tokens
-  int rsum[256];     // row_sum of the tile's tokens
-  float fac0[256];   // w_scale / row_scale per token (gate scale for RELU2_MUL)
-  float fac1[256];   // up scale / row_scale per token (RELU2_MUL)
+  // 16-byte aligned: the epilogue reads them as int4 / float4
+  alignas(16) float scale[256];  // row_scale of the tile's tokens
+  alignas(16) int rsum[256];     // row_sum of the tile's tokens
+  alignas(16) float fac0[256];   // w_scale / row_scale per token (gate scale for RELU2_MUL)
+  alignas(16) float fac1[256];   // up scale / row_scale per token (RELU2_MUL)
 };
 
 static_assert(sizeof(TcCtrl) <= TC_CTRL_BYTES, "control block");
+static_assert(offsetof(TcCtrl, rsum) % 16 == 0 && offsetof(TcCtrl, fac0) % 16 == 0 &&
+                  offsetof(TcCtrl, fac1) % 16 == 0,
+              "vector reads of the per-token arrays");
 
 template <int EPI>
 __global__ void __launch_bounds__(TC_THREADS, 2) bitlinear_tc_kernel(const TcParams p) {
@@ -206,23 +214,39 @@ __global__ void __launch_bounds__(TC_THREADS, 2) bitlinear_tc_kernel(const TcPar
       ctrl->scale[i] = p.row_scale[mg];
       ctrl->rsum[i] = p.row_sum[mg];
     }
-    if (lane == 0) {
-      // Refills (only when the K range has more stages than the ring has slots).
-      issued = pre;
+    // Refills (only when the K range has more stages than the ring has slots).
+    // Lane 0 waits for the slot; the warp stays converged, and a large
+    // activation block is split over XPARTS lanes: one thread's bulk copies
+    // complete one after another, several threads' copies overlap.
+    issued = pre;
+    {
       const uint64_t policy = l2_policy_evict_first();
       for (int s = pre; s < nstages; ++s) {
         const int slot = s % nslot;
         // the slot's previous stage (s - nslot) is fully consumed once its MMAs are done
-        if (!wait(&ctrl->slot_free[slot], ((s / nslot) + 1) & 1, 200)) break;
+        bool ok = true;
+        if (lane == 0) ok = wait(&ctrl->slot_free[slot], ((s / nslot) + 1) & 1, 200);
+        if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
         const int nch = stage_chunks(s), kc_s = kc0(s);
-        mbar_arrive_expect_tx(&ctrl->w_full[slot], (uint32_t)(nch * 2048));
-        bulk_g2s_stream(ring + (size_t)slot * slot_bytes, p.w + ((size_t)nb * KC + kc_s) * 2048u, nch * 2048,
-                        &ctrl->w_full[slot], policy);
-        mbar_arrive_expect_tx(&ctrl->x_full[slot], (uint32_t)(nch * 64 * T));
-        bulk_g2s(ring + (size_t)slot * slot_bytes + wslot_bytes,
-                 p.q + (size_t)mt * T * p.Kp + (size_t)kc_s * 64 * T, nch * 64 * T, &ctrl->x_full[slot]);
+        const uint32_t xbytes = (uint32_t)(nch * 64 * T);
+        const int xparts = xbytes >= 32768u ? 4 : 1;  // xbytes is a multiple of 1024
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&ctrl->w_full[slot], (uint32_t)(nch * 2048));
+          bulk_g2s_stream(ring + (size_t)slot * slot_bytes, p.w + ((size_t)nb * KC + kc_s) * 2048u, nch * 2048,
+                          &ctrl->w_full[slot], policy);
+          // armed with the whole block before any part is issued
+          mbar_arrive_expect_tx(&ctrl->x_full[slot], xbytes);
+        }
+        __syncwarp();
+        if (lane < xparts) {
+          const uint32_t part = xbytes / (uint32_t)xparts;
+          bulk_g2s(ring + (size_t)slot * slot_bytes + wslot_bytes + lane * part,
+                   p.q + (size_t)mt * T * p.Kp + (size_t)kc_s * 64 * T + lane * part, part, &ctrl->x_full[slot]);
+        }
         issued = s + 1;
       }
+    }
+    if (lane == 0) {
       if (*abort_flag) {
         for (int s = max(0, issued - nslot); s < issued; ++s) {
           mbar_wait(&ctrl->w_full[s % nslot], (s / nslot) & 1, 204);
@@ -312,6 +336,131 @@ __global__ void __launch_bounds__(TC_THREADS, 2) bitlinear_tc_kernel(const TcPar
       if (EPI == EPI_RELU2_MUL) ctrl->fac1[m] = __fdiv_rn(p.seg.scale[1], ctrl->scale[m]);
     }
   }
+  const int used_acc = min(NACC, 2 * (kc_end - kc_begin));
+
+  if (split == 1) {
+    // Whole-K tile: no exchange.  Phase 1: the unpacker warps read D (thread =
+    // weight row, 16 tokens per tcgen05.ld), finish each value to its bf16 result
+    // and stage it token-major in the (now idle) ring.  Phase 2: all 12 warps
+    // write whole output rows with 16-byte stores; the residual is read in
+    // batches of 4 vectors per thread before any of their stores, so the loads
+    // overlap (y and residual may be the same buffer, which keeps the compiler
+    // from moving a load above an earlier store).
+    uint16_t* st = reinterpret_cast<uint16_t*>(ring);  // [T][TC_ST_LD] bf16
+    __syncthreads();  // fac0 / fac1 visible
+    if (!*abort_flag) {
+      // all 12 warps: warp w reads TMEM lane quarter w % 4 (the rows it may
+      // access) and every third 16-token chunk
+      const int quarter = warp & 3, third = warp >> 2;
+      const int r = quarter * 32 + lane;  // TMEM lane = row of the weight tile
+      const int n = nb * 128 + r;
+      const uint32_t lanes = (uint32_t)(quarter * 32) << 16;
+      // RELU2_MUL rows: 0-31 gates of pairs 0-31, 32-63 their ups, 64-95 gates
+      // of pairs 32-63, 96-127 their ups; staged as [gates 0-63 | ups 0-63]
+      const bool up = (EPI == EPI_RELU2_MUL) && ((r >> 5) & 1);
+      const int col = (EPI == EPI_RELU2_MUL) ? (up ? 64 : 0) + (r & 31) + (r >> 6) * 32 : r;
+      const float* fac = up ? ctrl->fac1 : ctrl->fac0;
+      const float wsc = seg_scale_of(p.seg, n);
+      const bool fast = EPI == EPI_RELU2_MUL || seg_uniform;
+      for (int c = third * 16; c < T; c += 48) {
+        uint32_t sum[16];
+        tmem_ld16(tmem_d + lanes + c, sum);
+        tmem_wait_ld();
+        for (int a = 1; a < used_acc; ++a) {
+          uint32_t v[16];
+          tmem_ld16(tmem_d + lanes + a * T + c, v);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) sum[j] += v[j];
+        }
+        int acc[16];
+#pragma unroll
+        for (int j4 = 0; j4 < 4; ++j4) {
+          const int4 rs = *reinterpret_cast<const int4*>(&ctrl->rsum[c + 4 * j4]);
+          const float4 f4 = *reinterpret_cast<const float4*>(&fac[c + 4 * j4]);
+          const int rsv[4] = {rs.x, rs.y, rs.z, rs.w};
+          const float fv[4] = {f4.x, f4.y, f4.z, f4.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int j = 4 * j4 + e, m = c + j;
+            acc[j] = (int)sum[j] - rsv[e];
+            const float v = fast ? round_bf16(__fmul_rn((float)acc[j], fv[e])) : scaled_bf16(acc[j], wsc, ctrl->scale[m]);
+            st[m * TC_ST_LD + col] = f32_to_bf16_bits(v);
+          }
+        }
+        if (p.acc_out != nullptr && n < N) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int mg = mt * T + c + j;
+            if (mg < p.M) p.acc_out[(size_t)mg * N + n] = acc[j];
+          }
+        }
+      }
+    }
+    __syncthreads();
+    if (!*abort_flag) {
+      constexpr int NCOL = (EPI == EPI_RELU2_MUL) ? 64 : 128;  // outputs of one token in this tile
+      constexpr int CH = NCOL / 8;
+      const int Nout = (EPI == EPI_RELU2_MUL) ? (N >> 1) : N;
+      const int col0 = nb * NCOL;
+      const int ncols = min(NCOL, Nout - col0);
+      const int mvalid = min(T, p.M - mt * T);
+      const bool vec = ((Nout & 7) == 0) && ((reinterpret_cast<uintptr_t>(p.y) & 15) == 0) &&
+                       (EPI != EPI_RESIDUAL_ADD || (reinterpret_cast<uintptr_t>(p.residual) & 15) == 0);
+      const int items = mvalid * CH;
+      constexpr int BATCH = 4;
+      for (int i0 = tid; i0 < items; i0 += BATCH * TC_THREADS) {
+        uint4 res[BATCH];
+        if (EPI == EPI_RESIDUAL_ADD) {
+#pragma unroll
+          for (int u = 0; u < BATCH; ++u) {
+            const int it = i0 + u * TC_THREADS;
+            res[u] = make_uint4(0, 0, 0, 0);
+            if (it < items) {
+              const int m = it / CH, c0 = (it % CH) * 8;
+              const size_t o = (size_t)(mt * T + m) * Nout + col0 + c0;
+              if (vec && c0 + 8 <= ncols) {
+                res[u] = *reinterpret_cast<const uint4*>(p.residual + o);
+              } else {
+                uint16_t* rs = reinterpret_cast<uint16_t*>(&res[u]);
+                for (int e = 0; e < 8 && c0 + e < ncols; ++e) rs[e] = p.residual[o + e];
+              }
+            }
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < BATCH; ++u) {
+          const int it = i0 + u * TC_THREADS;
+          if (it >= items) break;
+          const int m = it / CH, c0 = (it % CH) * 8;
+          if (c0 >= ncols) continue;
+          const size_t o = (size_t)(mt * T + m) * Nout + col0 + c0;
+          const uint16_t* sv = st + m * TC_ST_LD + c0;
+          alignas(16) uint16_t out[8];
+          if (EPI == EPI_RELU2_MUL) {
+            const uint4 g4 = *reinterpret_cast<const uint4*>(sv);
+            const uint4 u4 = *reinterpret_cast<const uint4*>(sv + 64);
+            const uint16_t* g = reinterpret_cast<const uint16_t*>(&g4);
+            const uint16_t* uu = reinterpret_cast<const uint16_t*>(&u4);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) out[e] = relu2_mul_bf16(bf16_bits_to_f32(g[e]), bf16_bits_to_f32(uu[e]));
+          } else {
+            const uint4 v4 = *reinterpret_cast<const uint4*>(sv);
+            const uint16_t* v = reinterpret_cast<const uint16_t*>(&v4);
+            const uint16_t* rs = reinterpret_cast<const uint16_t*>(&res[u]);
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+              out[e] = (EPI == EPI_RESIDUAL_ADD) ? residual_add_bf16(rs[e], bf16_bits_to_f32(v[e])) : v[e];
+          }
+          if (vec && c0 + 8 <= ncols) {
+            *reinterpret_cast<uint4*>(p.y + o) = *reinterpret_cast<const uint4*>(out);
+          } else {
+            for (int e = 0; e < 8 && c0 + e < ncols; ++e) p.y[o + e] = out[e];
+          }
+        }
+      }
+    }
+  } else {
 
   // Partial D -> the owner of each token.  Rank j of the cluster owns tokens
   // [j * tok_cap, min(T, (j + 1) * tok_cap)).  A CTA writes the partials of
@@ -325,7 +474,6 @@ __global__ void __launch_bounds__(TC_THREADS, 2) bitlinear_tc_kernel(const TcPar
   int* recv = reinterpret_cast<int*>(split > 1 ? ring + (size_t)nslot * slot_bytes : ring);
   int* stage = recv + (size_t)split * 128 * ldr;
   if (split > 1) cluster_wait();  // every CTA of the cluster has started
-  const int used_acc = min(NACC, 2 * (kc_end - kc_begin));
   if (warp < TC_UNPACK_WARPS && !*abort_flag) {
     const int quarter = warp & 3, half = warp >> 2;
     const int row = quarter * 32 + lane;
@@ -429,6 +577,8 @@ __global__ void __launch_bounds__(TC_THREADS, 2) bitlinear_tc_kernel(const TcPar
       }
     }
   }
+
+  }  // split > 1
 
   if (split > 1 && tid < split) bulk_wait_group_read0();  // outgoing copies have read the staging area
   tc_fence_before();

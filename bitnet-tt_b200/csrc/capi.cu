@@ -194,7 +194,7 @@ int dispatch_simt(const int8_t* q, const float* rs, const int32_t* rsum, int M, 
 // peers wait for it.
 size_t tc_smem_bytes(int T, int nslot, int split, int cols = TC_TMEM_COLS) {
   const size_t ring = (size_t)nslot * tc_slot_bytes(T);
-  const size_t stage = (size_t)128 * (T + 1) * 4;
+  const size_t stage = (size_t)T * TC_ST_LD * 2;  // staged bf16 output tile (no K split)
   const size_t recv = (size_t)2 * split * tc_part_bytes(T, split);  // receive slots + staging
   size_t bytes = TC_CTRL_BYTES + (split > 1 ? ring + recv : (ring > stage ? ring : stage));
   const size_t floor_bytes = cols == 512 ? (size_t)116 * 1024 : (size_t)77 * 1024;
@@ -240,7 +240,10 @@ int dispatch_tc(TcParams p, int ntile_n, int ntile_m, bitnet_stream_t st, const 
     }
   }
   int cols = TC_TMEM_COLS;
-  if ((long)tiles * split > dev.sms && tc_nbuf(p.T, 256) >= 2) cols = 256;  // two CTAs per SM
+  // two CTAs per SM, when both the tensor memory and the shared memory of the
+  // smallest ring fit twice
+  if ((long)tiles * split > dev.sms && tc_nbuf(p.T, 256) >= 2 && tc_smem_bytes(p.T, 2, split, 256) <= tc_smem_limit(256))
+    cols = 256;
   if (split > 8 || split > p.KC) return BITNET_ERR_INVALID_ARGUMENT;
   if (split > 1 && p.T > 64) return BITNET_ERR_INVALID_ARGUMENT;
   const int nslot = tc_nslot(p.T, p.KC, split, cols);
@@ -362,8 +365,15 @@ int bitnet_act_quant(const void* x, int M, int K, int ldx, const void* gamma, fl
   if (q && !aligned(q, 16)) return BITNET_ERR_ALIGNMENT;
   const int Kp = round_up(K, 64);
   const int rows = want_q ? act_rows_of(M) : M;
-  if (K % 8 == 0 && ldx % 8 == 0 && Kp <= 8 * AQ_THREADS * AQ_MAXC && aligned(x, 16) &&
-      (!gamma || aligned(gamma, 16)) && (!normed_out || aligned(normed_out, 16)))
+  const bool vec_ok = K % 8 == 0 && ldx % 8 == 0 && aligned(x, 16) && (!gamma || aligned(gamma, 16)) &&
+                      (!normed_out || aligned(normed_out, 16));
+  // many rows: a warp per row (the rows are padded to whole token tiles, multiples of 8)
+  if (vec_ok && M >= 256 && rows % 8 == 0) {
+    auto k = Kp <= 8 * 32 * 10 ? act_quant_warp_kernel<10> : act_quant_warp_stream_kernel;
+    return launch(k, dim3(rows / 8), dim3(256), 0, stream, 1, (const uint16_t*)x, M, K, ldx, (const uint16_t*)gamma,
+                  eps, q, row_scale, row_sum, (uint16_t*)normed_out, act_tile_of(M), Kp);
+  }
+  if (vec_ok && Kp <= 8 * AQ_THREADS * AQ_MAXC)
     return launch(act_quant_vec_kernel, dim3(rows), dim3(AQ_THREADS), 0, stream, 1, (const uint16_t*)x, M, K, ldx,
                   (const uint16_t*)gamma, eps, q, row_scale, row_sum, (uint16_t*)normed_out, act_tile_of(M), Kp);
   const size_t smem = (size_t)Kp * 4;
@@ -507,7 +517,9 @@ int bitnet_rope_append_prefill(const void* qkv, int B, int P, int n_heads, int n
   if (B <= 0 || P <= 0 || n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads != 0 || head_dim != ATT_D ||
       P > max_len || P > rope_len)
     return BITNET_ERR_INVALID_ARGUMENT;
-  if (!aligned(qkv, 2) || !aligned(q_out, 2) || !aligned(k_cache, 2) || !aligned(v_cache, 2)) return BITNET_ERR_ALIGNMENT;
+  if (!aligned(qkv, 4) || !aligned(q_out, 4) || !aligned(k_cache, 4) || !aligned(v_cache, 4) || !aligned(rope_cos, 4) ||
+      !aligned(rope_sin, 4))
+    return BITNET_ERR_ALIGNMENT;
   RopePrefillParams p;
   p.qkv = (const uint16_t*)qkv;
   p.B = B;
@@ -520,9 +532,8 @@ int bitnet_rope_append_prefill(const void* qkv, int B, int P, int n_heads, int n
   p.k_cache = (uint16_t*)k_cache;
   p.v_cache = (uint16_t*)v_cache;
   p.max_len = max_len;
-  const size_t total = (size_t)B * P * (n_heads + n_kv_heads) * 64;
-  const int grid = (int)std::min<size_t>((total + 255) / 256, (size_t)d->sms * 16);
-  return launch(rope_append_prefill_kernel, dim3(grid), dim3(256), 0, stream, 1, p);
+  if ((long long)B * P > 0x7fffffffLL) return BITNET_ERR_INVALID_ARGUMENT;
+  return launch(rope_append_prefill_kernel, dim3(B * P), dim3(256), 0, stream, 1, p);
 }
 
 int bitnet_attention_prefill(const void* q, const void* k_cache, const void* v_cache, int B, int P, int n_heads,

@@ -68,7 +68,9 @@ def run_act_quant(x: torch.Tensor, gamma: torch.Tensor | None, eps: float, cuda)
 
 
 @pytest.mark.parametrize("m,k", [(1, 64), (3, 100), (8, 2560), (32, 2560), (32, 6912), (40, 320), (300, 128),
-                                 (2, 8192), (2, 8200)])
+                                 (2, 8192), (2, 8200),
+                                 # many rows: one warp per row (prefill), both register budgets, ragged last tile
+                                 (260, 2560), (520, 6912), (1024, 7168), (256, 8192)])
 @pytest.mark.parametrize("with_gamma", [True, False])
 def test_act_quant_bit_exact(cuda, m, k, with_gamma):
     x = rand_bf16((m, k), seed=m * 1000 + k)
@@ -177,6 +179,8 @@ def test_bitlinear_epilogues(cuda, path, epilogue, m):
     (32, 13824, 2560, "relu2_mul", 2),    # gate_up shape, 216 CTAs: two per SM, 256 TMEM columns
     (32, 2560, 6912, "residual_add", 8),  # down shape, 160 CTAs
     (16, 2560, 2560, "residual_add", 8),  # token tile 16
+    (64, 2560, 2560, "residual_add", 0),  # 64 tokens, automatic split: one CTA per SM (shared memory)
+    (64, 13824, 2560, "relu2_mul", 0),
 ])
 def test_bitlinear_tcgen05_decode_shapes(cuda, m, n, k, epilogue, split):
     check_bitlinear(cuda, m, n, k, path=2, epilogue=epilogue, seed=n + k, split=split)

@@ -3,7 +3,10 @@ the CPU oracle (through the product API, which calls the C ABI).
 
 Tolerances: attention output within 2e-2 (fp32 softmax in a different order,
 bf16 output); logits within 2e-2 relative (BASELINE); greedy tokens equal
-except at documented near-ties (top-2 oracle logits within 2 bf16 ulps)."""
+except at documented near-ties: on identical inputs, top-2 oracle logits
+within 2 bf16 ulps; after steps on the device's own KV cache (whose bf16
+rows differ from the oracle's by rounding), the oracle logits of the two
+tokens within the logits tolerance (2e-2 of the row's largest logit)."""
 
 import numpy as np
 import pytest
@@ -317,6 +320,18 @@ def _near_tie(logits: torch.Tensor) -> torch.Tensor:
     return (top2[:, 0] - top2[:, 1]) <= 2 * ulp
 
 
+def _within_logit_tol(ref_row: torch.Tensor, dev_id: int) -> tuple[bool, str]:
+    """A greedy mismatch after decoding on a device's own KV cache: allowed when
+    the oracle logits of its token and of the device's token differ by less
+    than the logits tolerance (2e-2 of the row's largest magnitude) or by at
+    most 2 bf16 ulps."""
+    top = int(torch.argmax(ref_row))
+    gap = float(ref_row[top] - ref_row[dev_id])
+    scale = float(ref_row.abs().max())
+    ulp = 2.0 ** (np.floor(np.log2(max(abs(float(ref_row[top])), 1e-30))) - 7)
+    return gap <= max(2e-2 * scale, 2 * ulp), f"gap {gap:.4g}, row scale {scale:.4g}, ulp {ulp:.3g}"
+
+
 @pytest.mark.parametrize("batch", [4, 32])
 def test_small_model_decode_matches_oracle(cuda, batch):
     from bitnet_tt.inference import Batch32Generator
@@ -340,10 +355,20 @@ def test_small_model_decode_matches_oracle(cuda, batch):
     # first step: same inputs on both sides
     rel = (dev_logits[0] - ref_logits[0]).norm() / ref_logits[0].norm()
     assert rel < 2e-2, f"logits rel err {rel:.3e}"
+    # while the sequences agree, every step's logits (over those rows) are within tolerance
+    agree = np.ones(batch, dtype=bool)
+    for t in range(new):
+        rows = torch.from_numpy(np.nonzero(agree)[0])
+        if rows.numel():
+            d, r = dev_logits[t][rows], ref_logits[t][rows]
+            rr = (d - r).norm() / r.norm()
+            assert rr < 2e-2, f"step {t}: logits rel err {rr:.3e} over {rows.numel()} agreeing rows"
+        agree &= dev_tokens[:, t] == ref_tokens[:, t]
     for b in range(batch):
         for t in range(new):
             if dev_tokens[b, t] != ref_tokens[b, t]:
-                assert bool(_near_tie(ref_logits[t][b:b + 1])[0]), f"seq {b} step {t}: not a near-tie"
+                ok, why = _within_logit_tol(ref_logits[t][b], int(dev_tokens[b, t]))
+                assert ok, f"seq {b} step {t}: not a near-tie ({why})"
                 break  # the sequences legitimately diverge after a near-tie
 
 
