@@ -3,9 +3,11 @@ the seeded synthetic BitNet-2B-shaped state dicts used by the benches.
 
 load_bitnet_weights reads a local HF checkpoint directory (config.json +
 *.safetensors); converting keys, splitting per layer and loading into a model
-follow the reference functions of the same names.  No checkpoint ships with
-this build, so the benches and tests use synthetic_state_dict: a lazy mapping
-that generates each tensor from (seed, key) on first access.
+follow the reference functions of the same names.  save_hf_checkpoint writes
+such a directory; save_packed_weights / load_packed_weights cache a loaded
+model in its device layout.  No checkpoint ships with this build, so the
+benches and tests use synthetic_state_dict: a lazy mapping that generates each
+tensor from (seed, key) on first access.
 """
 
 from __future__ import annotations
@@ -98,6 +100,120 @@ def load_weights_to_model(model: Any, state_dict: Mapping[str, Any]) -> None:
     if "norm.weight" in state_dict:
         lm = state_dict["lm_head.weight"] if "lm_head.weight" in state_dict else None
         model.load_final_weights(state_dict["norm.weight"], lm)
+
+
+# ---------------------------------------------------------------------------
+# checkpoints on disk: HF layout in, packed device layout cached
+# ---------------------------------------------------------------------------
+def save_hf_checkpoint(state_dict: Mapping[str, Any], config: BitNetConfig, path: str,
+                       max_shard_bytes: int = 1 << 30) -> list[str]:
+    """Write a state dict with this package's keys as an HF checkpoint directory:
+    config.json plus bf16 ``model-XXXXX-of-YYYYY.safetensors`` shards with the HF
+    key names (the inverse of load_bitnet_weights).  No real checkpoint ships
+    with this build; tests and users write synthetic ones with it."""
+    from safetensors.torch import save_file
+
+    os.makedirs(path, exist_ok=True)
+    inv = {v: k for k, v in _TOP_LEVEL.items()}
+    tensors: list[tuple[str, torch.Tensor]] = []
+    for key in state_dict.keys():
+        hf_key = inv.get(key, "model." + key if key.startswith("layers.") else key)
+        v = state_dict[key]
+        t = v if isinstance(v, torch.Tensor) else torch.from_numpy(np.asarray(v, dtype=np.float32))
+        tensors.append((hf_key, t.detach().to("cpu", torch.bfloat16).contiguous()))
+    shards: list[list[tuple[str, torch.Tensor]]] = [[]]
+    size = 0
+    for name, t in tensors:
+        nb = t.numel() * t.element_size()
+        if shards[-1] and size + nb > max_shard_bytes:
+            shards.append([])
+            size = 0
+        shards[-1].append((name, t))
+        size += nb
+    files = []
+    for i, shard in enumerate(shards):
+        fname = f"model-{i + 1:05d}-of-{len(shards):05d}.safetensors"
+        save_file(dict(shard), os.path.join(path, fname), metadata={"format": "pt"})
+        files.append(fname)
+    hf = {"architectures": ["BitNetForCausalLM"], "hidden_size": config.hidden_size,
+          "num_hidden_layers": config.num_layers, "num_attention_heads": config.num_attention_heads,
+          "num_key_value_heads": config.num_key_value_heads, "intermediate_size": config.intermediate_size,
+          "vocab_size": config.vocab_size, "max_position_embeddings": config.max_position_embeddings,
+          "rms_norm_eps": config.rms_norm_eps, "rope_theta": config.rope_theta, "torch_dtype": "bfloat16"}
+    with open(os.path.join(path, "config.json"), "w") as f:
+        json.dump(hf, f, indent=1)
+    return files
+
+
+_PACKED_FORMAT = "bitnet-b200-packed-v1"
+
+
+def _model_parts(model: Any) -> Iterator[tuple[str, str, Any]]:
+    """(name, kind, object) of every device-resident weight of a model."""
+    for i, layer in enumerate(model.layers):
+        a, f = layer.self_attn, layer.mlp
+        for name, lin in (("self_attn.qkv_proj", a.qkv_proj), ("self_attn.o_proj", a.o_proj),
+                          ("mlp.gate_up_proj", f.gate_up_proj), ("mlp.down_proj", f.down_proj)):
+            yield f"layers.{i}.{name}", "linear", lin
+        for name, norm in (("input_layernorm", layer.input_layernorm),
+                           ("post_attention_layernorm", layer.post_attention_layernorm),
+                           ("self_attn.attn_sub_norm", a.attn_sub_norm), ("mlp.ffn_sub_norm", f.ffn_sub_norm)):
+            yield f"layers.{i}.{name}", "norm", norm
+    yield "norm", "norm", model.norm
+
+
+def save_packed_weights(model: Any, path: str) -> None:
+    """Cache a loaded model in its device layout (packed 2-bit ternary matrices,
+    per-tensor scales, bf16 norms, the core-matrix-tiled embedding / lm_head) as
+    one safetensors file, so that later loads skip quantisation and packing
+    (load_packed_weights).  The layout is this library's; the file records the
+    model shape and is rejected for any other."""
+    from safetensors.torch import save_file
+
+    tensors: dict[str, torch.Tensor] = {}
+    meta: dict[str, Any] = {"format": _PACKED_FORMAT, "config": dict(vars(model.config)), "linears": {}}
+    for name, kind, obj in _model_parts(model):
+        if kind == "linear":
+            tensors[name + ".packed"] = obj.weight.detach().cpu().contiguous()
+            meta["linears"][name] = {"scale": obj.weight_scale, "segments": obj._segments}
+        else:
+            tensors[name + ".weight"] = obj.weight.detach().cpu().contiguous()
+    tensors["embed_tokens.weight_tiled"] = model.embed_tokens.weight_tiled.detach().cpu().contiguous()
+    tied = model.lm_head_tiled is model.embed_tokens.weight_tiled
+    meta["tied_lm_head"] = tied
+    if not tied:
+        tensors["lm_head_tiled"] = model.lm_head_tiled.detach().cpu().contiguous()
+    save_file(tensors, path, metadata={"bitnet": json.dumps(meta)})
+
+
+def load_packed_weights(model: Any, path: str) -> None:
+    """Load a save_packed_weights file into a model of the same shape: the device
+    tensors are copied as they are (no quantisation, no packing kernels)."""
+    from safetensors import safe_open
+
+    with safe_open(path, framework="pt") as f:
+        meta = json.loads((f.metadata() or {}).get("bitnet", "{}"))
+        if meta.get("format") != _PACKED_FORMAT:
+            raise ValueError(f"{path}: not a packed BitNet weight file")
+        want = dict(vars(model.config))
+        got = meta["config"]
+        for key in ("hidden_size", "num_layers", "num_attention_heads", "num_key_value_heads", "intermediate_size",
+                    "vocab_size", "head_dim"):
+            if key in want and want.get(key) != got.get(key):
+                raise ValueError(f"{path}: {key} {got.get(key)} does not match the model's {want.get(key)}")
+        dev = model.device
+        for name, kind, obj in _model_parts(model):
+            if kind == "linear":
+                obj.weight = f.get_tensor(name + ".packed").to(dev)
+                info = meta["linears"][name]
+                obj.weight_scale = float(info["scale"])
+                obj._segments = [tuple(sg) for sg in info["segments"]] if info["segments"] else None
+                obj._use_packed_ternary = True
+            else:
+                obj.weight = f.get_tensor(name + ".weight").to(dev)
+        model.embed_tokens.weight_tiled = f.get_tensor("embed_tokens.weight_tiled").to(dev)
+        model.lm_head_tiled = (model.embed_tokens.weight_tiled if meta.get("tied_lm_head")
+                               else f.get_tensor("lm_head_tiled").to(dev))
 
 
 # ---------------------------------------------------------------------------

@@ -165,3 +165,28 @@ def test_oracle_batched_prefill_equals_token_by_token():
     assert torch.allclose(logits, step_logits, rtol=1e-2, atol=1e-2)
     for (k, v), (ks, vs) in zip(caches, step_caches):
         assert torch.allclose(k, ks, rtol=1e-2, atol=1e-2) and torch.allclose(v, vs, rtol=1e-2, atol=1e-2)
+
+
+def test_hf_checkpoint_round_trip(tmp_path):
+    """A synthetic checkpoint written in the HF layout (bf16 safetensors shards,
+    HF key names, config.json) loads back through load_bitnet_weights with the
+    reference's key conversion and config fields."""
+    import torch
+
+    from bitnet_tt.config import BitNetConfig
+    from bitnet_tt.utils.weights import load_bitnet_weights, save_hf_checkpoint, synthetic_state_dict
+
+    cfg = BitNetConfig(hidden_size=256, num_layers=2, num_attention_heads=2, num_key_value_heads=1,
+                       intermediate_size=512, vocab_size=300, rms_norm_eps=1e-5)
+    sd = synthetic_state_dict(cfg, 3)
+    files = save_hf_checkpoint(sd, cfg, str(tmp_path), max_shard_bytes=300_000)
+    assert len(files) > 1 and all(f.endswith(".safetensors") for f in files)
+    sd2, cfg2 = load_bitnet_weights(str(tmp_path))
+    assert sorted(sd2) == sorted(sd.keys())
+    for k in sd.keys():
+        ref = torch.as_tensor(np.asarray(sd[k], dtype=np.float32)).to(torch.bfloat16).float().numpy()
+        np.testing.assert_array_equal(sd2[k], ref)
+    for f in ("hidden_size", "num_layers", "num_attention_heads", "num_key_value_heads", "intermediate_size",
+              "vocab_size", "rms_norm_eps", "rope_theta"):
+        assert getattr(cfg2, f) == getattr(cfg, f), f
+    assert "layers.1.self_attn.attn_sub_norm.weight" in sd2 and "embed_tokens.weight" in sd2

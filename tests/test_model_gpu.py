@@ -475,3 +475,49 @@ def test_vocab_sharded_lm_head_equals_unsharded(cuda, b, nshard):
     assert torch.equal(ids, ref)
     assert int(ids[1]) == 0
     assert torch.equal(pos.cpu(), torch.ones(b, dtype=torch.int32))
+
+
+def test_checkpoint_and_packed_cache_load_identically(cuda, tmp_path):
+    """HF-layout safetensors -> load_bitnet_weights -> device packing gives the
+    same device tensors as loading the (bf16-rounded) state dict directly; the
+    packed cache (save_packed_weights / load_packed_weights) reproduces them
+    byte for byte without packing, and a model from it decodes the same ids."""
+    from bitnet_tt.inference import Batch32Generator
+    from bitnet_tt.model import create_model
+    from bitnet_tt.utils.weights import (load_bitnet_weights, load_packed_weights, save_hf_checkpoint,
+                                         save_packed_weights)
+
+    cfg = _small_cfg()
+    sd = {k: torch.from_numpy(v).to(torch.bfloat16).float().numpy() for k, v in _numpy_sd(cfg, seed=19).items()}
+    save_hf_checkpoint(sd, cfg, str(tmp_path / "ckpt"), max_shard_bytes=1 << 20)
+    sd2, cfg2 = load_bitnet_weights(str(tmp_path / "ckpt"))
+    direct = _device_model(cfg, sd, cuda)
+    from_ckpt = _device_model(cfg2, sd2, cuda)
+    save_packed_weights(from_ckpt, str(tmp_path / "packed.safetensors"))
+    cached = create_model(cfg2, cuda)
+    load_packed_weights(cached, str(tmp_path / "packed.safetensors"))
+
+    def tensors(m):
+        out = [m.embed_tokens.weight_tiled, m.lm_head_tiled, m.norm.weight]
+        for layer in m.layers:
+            a, f = layer.self_attn, layer.mlp
+            out += [a.qkv_proj.weight, a.o_proj.weight, f.gate_up_proj.weight, f.down_proj.weight,
+                    layer.input_layernorm.weight, layer.post_attention_layernorm.weight, a.attn_sub_norm.weight,
+                    f.ffn_sub_norm.weight]
+        return out
+
+    for m in (from_ckpt, cached):
+        for x, y in zip(tensors(direct), tensors(m)):
+            assert torch.equal(x, y)
+        for la, lb in zip(direct.layers, m.layers):
+            for pa, pb in ((la.self_attn.qkv_proj, lb.self_attn.qkv_proj), (la.mlp.gate_up_proj, lb.mlp.gate_up_proj),
+                           (la.mlp.down_proj, lb.mlp.down_proj)):
+                assert pa.segments().count == pb.segments().count
+                assert list(pa.segments().scale) == list(pb.segments().scale)
+    assert cached.lm_head_tiled is cached.embed_tokens.weight_tiled  # tied head stays one table
+    prompts = np.random.default_rng(4).integers(0, cfg.vocab_size, size=(4, 5))
+    ids = [Batch32Generator(m, batch_size=4, max_seq_len=32).generate(prompts, 4) for m in (direct, cached)]
+    np.testing.assert_array_equal(ids[0], ids[1])
+    other = create_model(_small_cfg(hidden_size=384, num_attention_heads=3, num_key_value_heads=1), cuda)
+    with pytest.raises(ValueError):
+        load_packed_weights(other, str(tmp_path / "packed.safetensors"))
