@@ -151,6 +151,12 @@ _SIGNATURES = {
     "bitnet_attention_prefill": (
         _c_int, [_c_void_p, _c_void_p, _c_void_p, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_float, _c_void_p,
                  _c_void_p]),
+    "bitnet_rope_append_prefill_varlen": (
+        _c_int, [_c_void_p, _c_int, _c_void_p, _c_int, _c_int, _c_int, _c_int, _c_int, _c_void_p, _c_void_p, _c_int,
+                 _c_void_p, _c_void_p, _c_void_p, _c_int, _c_void_p]),
+    "bitnet_attention_prefill_varlen": (
+        _c_int, [_c_void_p, _c_void_p, _c_void_p, _c_int, _c_void_p, _c_int, _c_int, _c_int, _c_int, _c_int, _c_float,
+                 _c_void_p, _c_void_p]),
     "bitnet_lm_head_bytes": (_c_size_t, [_c_int, _c_int]),
     "bitnet_pack_lm_head": (_c_int, [_c_void_p, _c_int, _c_int, _c_void_p, _c_void_p]),
     "bitnet_embed_gather": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_int, _c_int, _c_void_p, _c_void_p]),
@@ -443,3 +449,21 @@ def attention_prefill(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Ten
     check(load().bitnet_attention_prefill(ptr(q), ptr(k_cache), ptr(v_cache), b, p, n_heads, n_kv, 128,
                                           k_cache.shape[2], float(scale), ptr(out), stream_handle()),
           "bitnet_attention_prefill")
+
+
+def rope_append_prefill_varlen(qkv: torch.Tensor, cu_seqlens: torch.Tensor, max_seqlen: int, n_heads: int, n_kv: int,
+                               rope_cos: torch.Tensor, rope_sin: torch.Tensor, q_out: torch.Tensor,
+                               k_cache: torch.Tensor, v_cache: torch.Tensor) -> None:
+    b = cu_seqlens.numel() - 1
+    check(load().bitnet_rope_append_prefill_varlen(ptr(qkv), b, ptr(cu_seqlens), qkv.shape[0], int(max_seqlen), n_heads,
+                                                   n_kv, 128, ptr(rope_cos), ptr(rope_sin), rope_cos.shape[0],
+                                                   ptr(q_out), ptr(k_cache), ptr(v_cache), k_cache.shape[2],
+                                                   stream_handle()), "bitnet_rope_append_prefill_varlen")
+
+
+def attention_prefill_varlen(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, cu_seqlens: torch.Tensor,
+                             max_seqlen: int, n_heads: int, n_kv: int, scale: float, out: torch.Tensor) -> None:
+    b = cu_seqlens.numel() - 1
+    check(load().bitnet_attention_prefill_varlen(ptr(q), ptr(k_cache), ptr(v_cache), b, ptr(cu_seqlens),
+                                                 int(max_seqlen), n_heads, n_kv, 128, k_cache.shape[2], float(scale),
+                                                 ptr(out), stream_handle()), "bitnet_attention_prefill_varlen")

@@ -152,6 +152,7 @@ class Batch32Generator:
         self.prefill_buffers: PrefillBuffers | None = None
         # batched_prefill=False: every prompt token goes through the decode graph
         self.batched_prefill = True
+        self.prefill_chunk_tokens = 65536  # ragged prompts: tokens per prefill pass (bounds its buffers)
 
     def set_context_limit(self, n: int) -> None:
         """Bound the positions the next steps reach (positions + 1 <= n).  The
@@ -311,12 +312,71 @@ class Batch32Generator:
         else:
             self.vocab_head.step(st.normed, st.ids, st.positions)
 
+    def _prefill_ragged(self, prompts: list[np.ndarray]) -> None:
+        """Prompts of different lengths, packed without padding: sequences are
+        taken in groups of at most `prefill_chunk_tokens` tokens (a longer
+        prompt is a group of its own), and each group runs the prefill layers
+        with the varlen RoPE / attention kernels (token offsets cu_seqlens) on
+        its slice of the decode caches.  Then the final norm of every
+        sequence's last prompt token and the lm_head + argmax leave the first
+        generated ids in st.ids and each prompt's length in st.positions."""
+        st = self.state
+        m, cfg = self.model, self.config
+        eps = cfg.rms_norm_eps
+        nq, nkv = cfg.num_attention_heads, cfg.num_key_value_heads
+        lens = [int(p.size) for p in prompts]
+        groups, g0, tok = [], 0, 0
+        for b, n in enumerate(lens):
+            if b > g0 and tok + n > self.prefill_chunk_tokens:
+                groups.append((g0, b))
+                g0, tok = b, 0
+            tok += n
+        groups.append((g0, len(lens)))
+        cap = max(sum(lens[a:e]) for a, e in groups)
+        cap = cap if cap <= 256 else -(-cap // 256) * 256
+        if self.prefill_buffers is None or self.prefill_buffers.tokens < cap:
+            self.prefill_buffers = None
+            self.prefill_buffers = PrefillBuffers(m, cap)
+        pb = self.prefill_buffers
+        last = torch.empty((len(lens), cfg.hidden_size), dtype=torch.bfloat16, device=self.device)
+        for a, e in groups:
+            glens = np.array(lens[a:e], dtype=np.int64)
+            cu_h = np.zeros(e - a + 1, dtype=np.int32)
+            cu_h[1:] = np.cumsum(glens)
+            n = int(cu_h[-1])
+            cu = torch.from_numpy(cu_h).to(self.device)
+            pb.ids[:n].copy_(torch.from_numpy(np.concatenate(prompts[a:e]).astype(np.int32)))
+            hidden, qkv, q, attn_out, mid = pb.hidden[:n], pb.qkv[:n], pb.q[:n], pb.attn[:n], pb.mid[:n]
+            m.embed_tokens.gather_into(pb.ids[:n], hidden)
+            lmax = int(glens.max())
+            for layer, cache in zip(m.layers, st.caches):
+                at = layer.self_attn
+                kc, vc = cache.key_cache[a:e], cache.value_cache[a:e]
+                _lib.act_quant(hidden, layer.input_layernorm.weight, eps, pb.act_h)
+                at.qkv_proj.forward_into(pb.act_h, n, qkv)
+                _lib.rope_append_prefill_varlen(qkv, cu, lmax, nq, nkv, st.rope_cos, st.rope_sin, q, kc, vc)
+                _lib.attention_prefill_varlen(q, kc, vc, cu, lmax, nq, nkv, at.scale, attn_out)
+                _lib.act_quant(attn_out, at.attn_sub_norm.weight, eps, pb.act_h)
+                at.o_proj.forward_into(pb.act_h, n, hidden, residual=hidden)
+                _lib.act_quant(hidden, layer.post_attention_layernorm.weight, eps, pb.act_h)
+                layer.mlp.gate_up_proj.forward_into(pb.act_h, n, mid)
+                _lib.act_quant(mid, layer.mlp.ffn_sub_norm.weight, eps, pb.act_f)
+                layer.mlp.down_proj.forward_into(pb.act_f, n, hidden, residual=hidden)
+            last[a:e].copy_(hidden.index_select(0, cu[1:].long() - 1))
+        _lib.rmsnorm(last, m.norm.weight, eps, st.normed)
+        st.positions.copy_(torch.tensor(lens, dtype=torch.int32) - 1)
+        if self.vocab_head is None:
+            m.lm_head_argmax(st.normed, st.argmax_ws, st.ids, st.logits, st.positions)
+        else:
+            self.vocab_head.step(st.normed, st.ids, st.positions)
+
     def prefill(self, input_ids) -> np.ndarray:
-        """Consume the prompts (ragged prompts allowed).  The first min(len)
-        tokens of every prompt go through the batched prefill; the rest, per
-        sequence, through the decode step one token at a time.  Returns the
-        prompt lengths; afterwards st.ids holds each sequence's first generated
-        token and st.positions its next position."""
+        """Consume the prompts (ragged prompts allowed) in batched prefill
+        passes: equal lengths as one [B, L] pass, different lengths packed
+        (`_prefill_ragged`).  With batched_prefill = False every prompt token
+        goes through the decode step instead.  Returns the prompt lengths;
+        afterwards st.ids holds each sequence's first generated token and
+        st.positions its next position."""
         prompts = self._prompts(input_ids)
         lens = np.array([p.size for p in prompts])
         if int(lens.max()) >= self.max_seq_len:
@@ -327,12 +387,13 @@ class Batch32Generator:
         self.reset()
         st = self.state
         lmax, lmin = int(lens.max()), int(lens.min())
-        t0 = 0
         if self.batched_prefill:
-            self._prefill_batched(np.stack([p[:lmin] for p in prompts]))
             if lmin == lmax:
-                return lens
-            t0 = lmin  # st.ids holds the first generated ids of the shortest prompts
+                self._prefill_batched(np.stack(prompts))
+            else:
+                self._prefill_ragged(prompts)
+            return lens
+        t0 = 0
         table = np.zeros((lmax, self.batch_size), dtype=np.int32)
         for b, p in enumerate(prompts):
             table[: p.size, b] = p

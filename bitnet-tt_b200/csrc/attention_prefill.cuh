@@ -28,8 +28,10 @@ constexpr int APF_NBUF = 2;
 constexpr size_t APF_SMEM = (size_t)APF_NBUF * 2 * APF_KV_BYTES + 64;  // K|V x 2 buffers + 2 mbarriers
 
 struct RopePrefillParams {
-  const uint16_t* qkv;  // [B*P, (n_heads + 2 n_kv) * 128]
+  const uint16_t* qkv;  // [tokens, (n_heads + 2 n_kv) * 128]
   int B, P, n_heads, n_kv;
+  const int32_t* cu;    // nullable: sequence b owns tokens cu[b] .. cu[b+1]-1 (ragged prompts); else b*P ..
+  int rope_len;
   const uint16_t* rope_cos;  // [>= P, 64]
   const uint16_t* rope_sin;
   uint16_t* q_out;     // [B*P, n_heads * 128]
@@ -44,7 +46,24 @@ __global__ void __launch_bounds__(256) rope_append_prefill_kernel(const RopePref
   pdl_trigger();
   pdl_wait();
   const int tok = blockIdx.x;
-  const int pos = tok % p.P, b = tok / p.P;
+  int pos, b;
+  if (p.cu != nullptr) {
+    // the sequence holding this token: the last b with cu[b] <= tok
+    int lo = 0, hi = p.B;
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (p.cu[mid] <= tok) lo = mid; else hi = mid;
+    }
+    b = lo;
+    pos = tok - p.cu[b];
+    if (pos < 0 || tok >= p.cu[b + 1] || pos >= p.max_len || pos >= p.rope_len) {
+      if (threadIdx.x == 0) record_error(DEV_ERR_BOUNDS, 330);
+      return;
+    }
+  } else {
+    pos = tok % p.P;
+    b = tok / p.P;
+  }
   const int nh = p.n_heads + p.n_kv;  // heads that get a rotation
   const uint16_t* row = p.qkv + (size_t)tok * (size_t)((p.n_heads + 2 * p.n_kv) * ATT_D);
   const uint32_t* cs = reinterpret_cast<const uint32_t*>(p.rope_cos + (size_t)pos * 64);
@@ -84,9 +103,10 @@ struct AttnPrefillParams {
   const uint16_t* q;  // [B*P, n_heads*128] rotated
   const uint16_t* k_cache;
   const uint16_t* v_cache;
-  int B, P, n_heads, n_kv, max_len;
+  int B, P, n_heads, n_kv, max_len;  // P: the (longest) prompt length
   float scale;
-  uint16_t* out;  // [B*P, n_heads*128]
+  uint16_t* out;  // [tokens, n_heads*128]
+  const int32_t* cu;  // nullable: token offsets of ragged prompts (sequence b: cu[b] .. cu[b+1]-1)
 };
 
 // grid (ceil(P / 64), n_heads, B), 128 threads, APF_SMEM dynamic shared memory.
@@ -104,7 +124,19 @@ __global__ void __launch_bounds__(APF_THREADS) attention_prefill_kernel(const At
   __syncthreads();
   pdl_wait();
   const int q0 = qb * APF_QB;
-  const int qend = min(p.P, q0 + APF_QB);            // query rows of the CTA: [q0, qend)
+  // this sequence's prompt: P tokens from row tok0 of q / out
+  int P = p.P;
+  size_t tok0 = (size_t)b * p.P;
+  if (p.cu != nullptr) {
+    tok0 = (size_t)p.cu[b];
+    P = p.cu[b + 1] - p.cu[b];
+    if (P < 0 || P > p.P || P > p.max_len) {
+      if (t == 0 && qb == 0 && h == 0) record_error(DEV_ERR_BOUNDS, 331);
+      return;
+    }
+  }
+  if (q0 >= P) return;  // CTA-uniform; nothing issued yet
+  const int qend = min(P, q0 + APF_QB);               // query rows of the CTA: [q0, qend)
   const int nkb = (qend - 1) / APF_KB + 1;           // key blocks 0 .. the one holding the last query
   const size_t crow0 = ((size_t)b * p.n_kv + g) * p.max_len;
   const uint16_t* kc = p.k_cache + crow0 * ATT_D;
@@ -118,7 +150,7 @@ __global__ void __launch_bounds__(APF_THREADS) attention_prefill_kernel(const At
     for (int j = 0; j < 16; ++j) {
       const int q = t + APF_THREADS * j;  // 0 .. 2047
       const int tensor = q >> 10, row = (q >> 4) & 63, c = q & 15;
-      const bool in = k0 + row < p.P;
+      const bool in = k0 + row < P;
       const uint16_t* src = (tensor ? vc : kc) + (size_t)(k0 + (in ? row : 0)) * ATT_D + c * 8;
       cp_async16_zfill(base + tensor * APF_KV_BYTES + att_swz(row, c), src, in ? 16u : 0u);
     }
@@ -131,8 +163,8 @@ __global__ void __launch_bounds__(APF_THREADS) attention_prefill_kernel(const At
   const int row_a = q0 + warp * 16 + qr, row_b = row_a + 8;
   uint32_t qa[8][4];
   {
-    const uint16_t* qa_row = p.q + ((size_t)b * p.P + min(row_a, p.P - 1)) * (size_t)(p.n_heads * ATT_D) + h * ATT_D;
-    const uint16_t* qb_row = p.q + ((size_t)b * p.P + min(row_b, p.P - 1)) * (size_t)(p.n_heads * ATT_D) + h * ATT_D;
+    const uint16_t* qa_row = p.q + (tok0 + min(row_a, P - 1)) * (size_t)(p.n_heads * ATT_D) + h * ATT_D;
+    const uint16_t* qb_row = p.q + (tok0 + min(row_b, P - 1)) * (size_t)(p.n_heads * ATT_D) + h * ATT_D;
 #pragma unroll
     for (int ks = 0; ks < 8; ++ks) {
       qa[ks][0] = *reinterpret_cast<const uint32_t*>(qa_row + 16 * ks + qc);
@@ -181,10 +213,10 @@ __global__ void __launch_bounds__(APF_THREADS) attention_prefill_kernel(const At
 #pragma unroll
     for (int n = 0; n < 8; ++n) {
       const int kk = k0 + 8 * n + qc;
-      s[n][0] = (kk <= row_a && kk < p.P) ? s[n][0] * p.scale : -INFINITY;
-      s[n][1] = (kk + 1 <= row_a && kk + 1 < p.P) ? s[n][1] * p.scale : -INFINITY;
-      s[n][2] = (kk <= row_b && kk < p.P) ? s[n][2] * p.scale : -INFINITY;
-      s[n][3] = (kk + 1 <= row_b && kk + 1 < p.P) ? s[n][3] * p.scale : -INFINITY;
+      s[n][0] = (kk <= row_a && kk < P) ? s[n][0] * p.scale : -INFINITY;
+      s[n][1] = (kk + 1 <= row_a && kk + 1 < P) ? s[n][1] * p.scale : -INFINITY;
+      s[n][2] = (kk <= row_b && kk < P) ? s[n][2] * p.scale : -INFINITY;
+      s[n][3] = (kk + 1 <= row_b && kk + 1 < P) ? s[n][3] * p.scale : -INFINITY;
       mxa = fmaxf(mxa, fmaxf(s[n][0], s[n][1]));
       mxb = fmaxf(mxb, fmaxf(s[n][2], s[n][3]));
     }
@@ -258,13 +290,13 @@ __global__ void __launch_bounds__(APF_THREADS) attention_prefill_kernel(const At
   if (!ok) return;
   // normalise and write rows row_a / row_b, dims 8 j + qc, + 1
   const float ia = l_a > 0.f ? 1.f / l_a : 0.f, ib = l_b > 0.f ? 1.f / l_b : 0.f;
-  uint16_t* oa = p.out + ((size_t)b * p.P + row_a) * (size_t)(p.n_heads * ATT_D) + h * ATT_D;
-  uint16_t* ob = p.out + ((size_t)b * p.P + row_b) * (size_t)(p.n_heads * ATT_D) + h * ATT_D;
+  uint16_t* oa = p.out + (tok0 + row_a) * (size_t)(p.n_heads * ATT_D) + h * ATT_D;
+  uint16_t* ob = p.out + (tok0 + row_b) * (size_t)(p.n_heads * ATT_D) + h * ATT_D;
 #pragma unroll
   for (int j = 0; j < 16; ++j) {
-    if (row_a < p.P)
+    if (row_a < P)
       *reinterpret_cast<uint32_t*>(oa + 8 * j + qc) = pack_bf16x2(o[j][0] * ia, o[j][1] * ia);
-    if (row_b < p.P)
+    if (row_b < P)
       *reinterpret_cast<uint32_t*>(ob + 8 * j + qc) = pack_bf16x2(o[j][2] * ib, o[j][3] * ib);
   }
 }

@@ -508,46 +508,67 @@ int bitnet_gqa_decode_attention(const void* qkv, int B, int n_heads, int n_kv_he
   }
 }
 
-int bitnet_rope_append_prefill(const void* qkv, int B, int P, int n_heads, int n_kv_heads, int head_dim,
-                               const void* rope_cos, const void* rope_sin, int rope_len, void* q_out, void* k_cache,
-                               void* v_cache, int max_len, bitnet_stream_t stream) {
+static int rope_prefill_impl(const void* qkv, int B, int P, const int32_t* cu, int tokens, int n_heads,
+                             int n_kv_heads, int head_dim, const void* rope_cos, const void* rope_sin, int rope_len,
+                             void* q_out, void* k_cache, void* v_cache, int max_len, bitnet_stream_t stream) {
   DevInfo* d;
   if (int e = device_info(&d)) return e;
   if (!qkv || !rope_cos || !rope_sin || !q_out || !k_cache || !v_cache) return BITNET_ERR_INVALID_ARGUMENT;
-  if (B <= 0 || P <= 0 || n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads != 0 || head_dim != ATT_D ||
-      P > max_len || P > rope_len)
+  if (B <= 0 || P <= 0 || tokens <= 0 || n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads != 0 ||
+      head_dim != ATT_D || P > max_len || P > rope_len)
     return BITNET_ERR_INVALID_ARGUMENT;
   if (!aligned(qkv, 4) || !aligned(q_out, 4) || !aligned(k_cache, 4) || !aligned(v_cache, 4) || !aligned(rope_cos, 4) ||
-      !aligned(rope_sin, 4))
+      !aligned(rope_sin, 4) || (cu && !aligned(cu, 4)))
     return BITNET_ERR_ALIGNMENT;
   RopePrefillParams p;
+  memset(&p, 0, sizeof(p));
   p.qkv = (const uint16_t*)qkv;
   p.B = B;
   p.P = P;
   p.n_heads = n_heads;
   p.n_kv = n_kv_heads;
+  p.cu = cu;
+  p.rope_len = rope_len;
   p.rope_cos = (const uint16_t*)rope_cos;
   p.rope_sin = (const uint16_t*)rope_sin;
   p.q_out = (uint16_t*)q_out;
   p.k_cache = (uint16_t*)k_cache;
   p.v_cache = (uint16_t*)v_cache;
   p.max_len = max_len;
-  if ((long long)B * P > 0x7fffffffLL) return BITNET_ERR_INVALID_ARGUMENT;
-  return launch(rope_append_prefill_kernel, dim3(B * P), dim3(256), 0, stream, 1, p);
+  return launch(rope_append_prefill_kernel, dim3(tokens), dim3(256), 0, stream, 1, p);
 }
 
-int bitnet_attention_prefill(const void* q, const void* k_cache, const void* v_cache, int B, int P, int n_heads,
-                             int n_kv_heads, int head_dim, int max_len, float scale, void* out,
-                             bitnet_stream_t stream) {
+int bitnet_rope_append_prefill(const void* qkv, int B, int P, int n_heads, int n_kv_heads, int head_dim,
+                               const void* rope_cos, const void* rope_sin, int rope_len, void* q_out, void* k_cache,
+                               void* v_cache, int max_len, bitnet_stream_t stream) {
+  if (B <= 0 || P <= 0 || (long long)B * P > 0x7fffffffLL) return BITNET_ERR_INVALID_ARGUMENT;
+  return rope_prefill_impl(qkv, B, P, nullptr, B * P, n_heads, n_kv_heads, head_dim, rope_cos, rope_sin, rope_len,
+                           q_out, k_cache, v_cache, max_len, stream);
+}
+
+int bitnet_rope_append_prefill_varlen(const void* qkv, int B, const int32_t* cu_seqlens, int total_tokens,
+                                      int max_seqlen, int n_heads, int n_kv_heads, int head_dim,
+                                      const void* rope_cos, const void* rope_sin, int rope_len, void* q_out,
+                                      void* k_cache, void* v_cache, int max_len, bitnet_stream_t stream) {
+  if (!cu_seqlens) return BITNET_ERR_INVALID_ARGUMENT;
+  return rope_prefill_impl(qkv, B, max_seqlen, cu_seqlens, total_tokens, n_heads, n_kv_heads, head_dim, rope_cos,
+                           rope_sin, rope_len, q_out, k_cache, v_cache, max_len, stream);
+}
+
+static int attention_prefill_impl(const void* q, const void* k_cache, const void* v_cache, int B, int P,
+                                  const int32_t* cu, int n_heads, int n_kv_heads, int head_dim, int max_len,
+                                  float scale, void* out, bitnet_stream_t stream) {
   DevInfo* d;
   if (int e = device_info(&d)) return e;
   if (!q || !k_cache || !v_cache || !out) return BITNET_ERR_INVALID_ARGUMENT;
   if (B <= 0 || P <= 0 || n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads != 0 || head_dim != ATT_D ||
-      P > max_len)
+      P > max_len || B > 65535)
     return BITNET_ERR_INVALID_ARGUMENT;
-  if (!aligned(q, 4) || !aligned(out, 4) || !aligned(k_cache, 16) || !aligned(v_cache, 16)) return BITNET_ERR_ALIGNMENT;
+  if (!aligned(q, 4) || !aligned(out, 4) || !aligned(k_cache, 16) || !aligned(v_cache, 16) || (cu && !aligned(cu, 4)))
+    return BITNET_ERR_ALIGNMENT;
   if (int e = ensure_smem(attention_prefill_kernel, &g_smem_apf)) return e;
   AttnPrefillParams p;
+  memset(&p, 0, sizeof(p));
   p.q = (const uint16_t*)q;
   p.k_cache = (const uint16_t*)k_cache;
   p.v_cache = (const uint16_t*)v_cache;
@@ -558,8 +579,24 @@ int bitnet_attention_prefill(const void* q, const void* k_cache, const void* v_c
   p.max_len = max_len;
   p.scale = scale;
   p.out = (uint16_t*)out;
+  p.cu = cu;
   return launch(attention_prefill_kernel, dim3((P + APF_QB - 1) / APF_QB, n_heads, B), dim3(APF_THREADS), APF_SMEM,
                 stream, 1, p);
+}
+
+int bitnet_attention_prefill(const void* q, const void* k_cache, const void* v_cache, int B, int P, int n_heads,
+                             int n_kv_heads, int head_dim, int max_len, float scale, void* out,
+                             bitnet_stream_t stream) {
+  return attention_prefill_impl(q, k_cache, v_cache, B, P, nullptr, n_heads, n_kv_heads, head_dim, max_len, scale, out,
+                                stream);
+}
+
+int bitnet_attention_prefill_varlen(const void* q, const void* k_cache, const void* v_cache, int B,
+                                    const int32_t* cu_seqlens, int max_seqlen, int n_heads, int n_kv_heads,
+                                    int head_dim, int max_len, float scale, void* out, bitnet_stream_t stream) {
+  if (!cu_seqlens) return BITNET_ERR_INVALID_ARGUMENT;
+  return attention_prefill_impl(q, k_cache, v_cache, B, max_seqlen, cu_seqlens, n_heads, n_kv_heads, head_dim,
+                                max_len, scale, out, stream);
 }
 
 size_t bitnet_lm_head_bytes(int V, int K) {

@@ -248,6 +248,18 @@ int bitnet_rope_append_prefill(const void* qkv, int B, int P, int n_heads, int n
 int bitnet_attention_prefill(const void* q, const void* k_cache, const void* v_cache, int B, int P, int n_heads,
                              int n_kv_heads, int head_dim, int max_len, float scale, void* out,
                              bitnet_stream_t stream);
+/* Ragged prompts: sequence b owns the packed token rows cu_seqlens[b] ..
+ * cu_seqlens[b+1]-1 (int32 [B+1] on the device, cu_seqlens[0] = 0,
+ * cu_seqlens[B] = total_tokens), at positions 0 .. its length - 1; max_seqlen
+ * bounds every length (it sizes the grid).  A length beyond max_seqlen /
+ * max_len / rope_len is a device bounds error (bitnet_last_device_status). */
+int bitnet_rope_append_prefill_varlen(const void* qkv, int B, const int32_t* cu_seqlens, int total_tokens,
+                                      int max_seqlen, int n_heads, int n_kv_heads, int head_dim,
+                                      const void* rope_cos, const void* rope_sin, int rope_len, void* q_out,
+                                      void* k_cache, void* v_cache, int max_len, bitnet_stream_t stream);
+int bitnet_attention_prefill_varlen(const void* q, const void* k_cache, const void* v_cache, int B,
+                                    const int32_t* cu_seqlens, int max_seqlen, int n_heads, int n_kv_heads,
+                                    int head_dim, int max_len, float scale, void* out, bitnet_stream_t stream);
 
 /* ---- lm_head / embedding table -------------------------------------------
  * The tied embedding / lm_head matrix (src/bitnet_tt/utils/weights.py:236-246)

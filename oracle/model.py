@@ -208,6 +208,17 @@ class OracleBitNet:
         logits = bf(rmsnorm(last, self.norm, self.eps) @ self.lm_head.t())
         return torch.argmax(logits, dim=-1).to(torch.int32), logits
 
+    def prefill_ragged(self, prompts: list[np.ndarray], caches) -> tuple[torch.Tensor, torch.Tensor]:
+        """Prompts of different lengths: each sequence through prefill() on its
+        own rows of the caches (the rows of one sequence never meet another's:
+        per-token quantisation, attention within the sequence)."""
+        ids, logits = [], []
+        for b, p in enumerate(prompts):
+            i, lg = self.prefill(np.asarray(p).reshape(1, -1), [(k[b:b + 1], v[b:b + 1]) for k, v in caches])
+            ids.append(i)
+            logits.append(lg)
+        return torch.cat(ids), torch.cat(logits)
+
     def step(self, ids: torch.Tensor, pos: torch.Tensor, caches) -> tuple[torch.Tensor, torch.Tensor]:
         """One greedy decode step: (next ids [B], bf16-valued logits [B, V])."""
         h = self.embed[ids.long()]

@@ -205,38 +205,89 @@ def test_batched_prefill_matches_oracle(cuda, batch, plen):
             assert (d - ref[:, :, :plen]).norm() / ref[:, :, :plen].norm() < 2e-2
 
 
-def test_ragged_prompts_batched_prefill_equals_decode_prefill(cuda):
-    """Ragged prompts: the shortest length in one batched pass, the rest by the
-    decode graph -- against every prompt token through the decode graph."""
+@pytest.mark.parametrize("chunk", [20, 65536])
+def test_ragged_prompts_prefill_matches_oracle(cuda, chunk):
+    """Ragged prompts packed without padding (varlen RoPE / attention; chunk 20
+    splits the batch into several prefill passes) against the oracle prefilling
+    each sequence on its own; then decode steps at the sequences' own positions."""
     from bitnet_tt.inference import Batch32Generator
 
     cfg = _small_cfg()
     sd = _numpy_sd(cfg, seed=5)
     model = _device_model(cfg, sd, cuda)
     rng = np.random.default_rng(3)
-    lens = [5, 12, 9, 5, 17, 6, 5, 8]
+    lens = [5, 12, 9, 1, 17, 6, 70, 8]
     prompts = [rng.integers(0, cfg.vocab_size, size=n) for n in lens]
-    runs = []
-    for batched in (True, False):
-        gen = Batch32Generator(model, batch_size=len(lens), max_seq_len=64, keep_logits=True)
-        gen.batched_prefill = batched
-        gen.prefill(prompts)
-        ids, logits = [gen.state.ids.cpu().numpy().copy()], [gen.state.logits.float().cpu().clone()]
-        for _ in range(4):
-            gen.step()
-            ids.append(gen.state.ids.cpu().numpy().copy())
-            logits.append(gen.state.logits.float().cpu().clone())
-        # every sequence steps with the batch: the shorter ones generate while the longer finish their prompts
-        assert gen.state.positions.cpu().tolist() == [max(lens) + 4] * len(lens)
-        runs.append((np.stack(ids, 1), logits))
-    (ta, la), (tb, lb) = runs
-    rel = (la[0] - lb[0]).norm() / lb[0].norm()
+    gen = Batch32Generator(model, batch_size=len(lens), max_seq_len=96, keep_logits=True)
+    gen.prefill_chunk_tokens = chunk
+    gen.prefill(prompts)
+    assert gen.state.positions.cpu().tolist() == lens
+    ids, logits = [gen.state.ids.cpu().numpy().copy()], [gen.state.logits.float().cpu().clone()]
+    for _ in range(3):
+        gen.step()
+        ids.append(gen.state.ids.cpu().numpy().copy())
+        logits.append(gen.state.logits.float().cpu().clone())
+    assert gen.state.positions.cpu().tolist() == [n + 3 for n in lens]
+    dev_ids = np.stack(ids, 1)
+
+    oracle = om.OracleBitNet(cfg, sd, max_len=96)
+    caches = oracle.new_cache(len(lens))
+    ref_first, ref_logits0 = oracle.prefill_ragged(prompts, caches)
+    c0 = gen.state.caches[0]
+    for b, n in enumerate(lens):  # layer 0 sees identical inputs: its K/V rows are bit-exact
+        assert torch.equal(c0.key_cache[b, :, :n].float().cpu(), caches[0][0][b, :, :n])
+        assert torch.equal(c0.value_cache[b, :, :n].float().cpu(), caches[0][1][b, :, :n])
+    rel = (logits[0] - ref_logits0).norm() / ref_logits0.norm()
     assert rel < 2e-2, f"logits rel err {rel:.3e}"
+    ref_ids, ref_logits = [ref_first.numpy()], [ref_logits0]
+    pos = torch.tensor(lens, dtype=torch.int32)
+    cur = ref_first
+    for _ in range(3):
+        cur, lg = oracle.step(cur, pos, caches)
+        pos = pos + 1
+        ref_ids.append(cur.numpy())
+        ref_logits.append(lg)
+    ref_ids = np.stack(ref_ids, 1)
     for b in range(len(lens)):
-        for t in range(ta.shape[1]):
-            if ta[b, t] != tb[b, t]:
-                assert bool(_near_tie(lb[t][b:b + 1])[0]), f"seq {b} step {t}: not a near-tie"
+        for t in range(dev_ids.shape[1]):
+            if dev_ids[b, t] != ref_ids[b, t]:
+                ok, why = _within_logit_tol(ref_logits[t][b], int(dev_ids[b, t]))
+                assert ok, f"seq {b} step {t}: not a near-tie ({why})"
                 break
+
+
+def test_attention_prefill_varlen_matches_oracle(cuda):
+    """Varlen RoPE / K-V append and causal attention on packed ragged prompts
+    against the oracle's prefill attention of each sequence alone."""
+    from bitnet_tt import _lib
+    from bitnet_tt.utils.rope import half_split_tables
+
+    lens = [1, 70, 129, 64, 300, 2]
+    nh, nkv, d, max_len = 8, 2, 128, 320
+    b = len(lens)
+    cu_h = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    n = int(cu_h[-1])
+    g = torch.Generator().manual_seed(23)
+    qkv = torch.randn((n, (nh + 2 * nkv) * d), generator=g).to(torch.bfloat16)
+    kc = torch.randn((b, nkv, max_len, d), generator=g).to(torch.bfloat16)
+    vc = torch.randn((b, nkv, max_len, d), generator=g).to(torch.bfloat16)
+    cos, sin = half_split_tables(d, max_len, 500000.0)
+    kd, vd = kc.to(cuda), vc.to(cuda)
+    q = torch.empty((n, nh * d), dtype=torch.bfloat16, device=cuda)
+    out = torch.empty((n, nh * d), dtype=torch.bfloat16, device=cuda)
+    cu = torch.from_numpy(cu_h).to(cuda)
+    _lib.rope_append_prefill_varlen(qkv.to(cuda), cu, max(lens), nh, nkv, cos.to(cuda), sin.to(cuda), q, kd, vd)
+    _lib.attention_prefill_varlen(q, kd, vd, cu, max(lens), nh, nkv, d ** -0.5, out)
+    torch.cuda.synchronize()
+    assert _lib.last_device_status()[0] == 0
+    o = om.OracleBitNet.__new__(om.OracleBitNet)
+    o.d, o.nq, o.nkv = d, nh, nkv
+    o.cos, o.sin = om.rope_tables(d, max_len, 500000.0)
+    kr, vr = kc.float().clone(), vc.float().clone()
+    for i, L in enumerate(lens):
+        ref = o.prefill_attention(qkv.float()[cu_h[i]:cu_h[i + 1]], 1, L, (kr[i:i + 1], vr[i:i + 1]))
+        np.testing.assert_allclose(out[cu_h[i]:cu_h[i + 1]].float().cpu().numpy(), ref.numpy(), rtol=2e-2, atol=2e-2)
+    assert torch.equal(kd.float().cpu(), kr) and torch.equal(vd.float().cpu(), vr)  # rows beyond each length untouched
 
 
 def test_full_width_prefill_matches_oracle(cuda):
