@@ -93,13 +93,17 @@ def roofline_groups(rl: dict, hbm_peak: float) -> dict:
 def parse() -> argparse.Namespace:
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--workload", choices=["config2", "config4"], default="config2",
+                   help="config2: 32 sequences per GPU, 64-token prompts (weak scaling, the headline); config4: "
+                        "--sequences split over the GPUs, ragged contexts U[128, 4096], 256 new tokens (strong scaling)")
+    p.add_argument("--sequences", type=int, default=256, help="config4: sequences over all GPUs")
     p.add_argument("--steps", type=int, default=1024)
     p.add_argument("--warmup", type=int, default=8)
     p.add_argument("--impl", choices=["b200", "reference"], default="b200")
     p.add_argument("--batch", type=int, default=32)
     p.add_argument("--prompt-len", type=int, default=64)
-    p.add_argument("--new-tokens", type=int, default=128)
-    p.add_argument("--max-seq-len", type=int, default=2048)
+    p.add_argument("--new-tokens", type=int, default=None, help="default 128 (config2) / 256 (config4)")
+    p.add_argument("--max-seq-len", type=int, default=None, help="default 2048 (config2) / 4352 (config4)")
     p.add_argument("--layers", type=int, default=30)
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--e2e-steps", type=int, default=256)
@@ -477,26 +481,42 @@ def run_b200(args) -> None:
     torch.cuda.synchronize(device)
     t_build = time.perf_counter() - t_build
 
-    b = args.batch
+    c4 = args.workload == "config4"
+    if c4 and args.sequences % world != 0:
+        raise SystemExit("--sequences must be a multiple of the GPU count")
+    b = args.sequences // world if c4 else args.batch
     shard = args.vocab_shard and world > 1
     import torch.distributed as dist  # noqa: F811 - only used when world > 1
 
     gen = Batch32Generator(model, batch_size=b, max_seq_len=args.max_seq_len,
                            persistent=args.decode_path == "persistent",
                            vocab_shard_group=dist.group.WORLD if shard else None)
-    gen.set_context_limit(args.prompt_len + args.new_tokens)  # positions cycle within it
-    rng = np.random.default_rng(args.seed * 1000 + rank)
-    prompts = rng.integers(0, cfg.vocab_size, size=(b, args.prompt_len))
+    if c4:
+        # ragged contexts: all --sequences lengths drawn from one seeded stream, each rank takes its slice
+        lens_all = np.random.default_rng(args.seed).integers(128, 4097, size=args.sequences)
+        lens = lens_all[rank * b:(rank + 1) * b]
+        rng = np.random.default_rng(args.seed * 1000 + rank)
+        prompts = [rng.integers(0, cfg.vocab_size, size=int(n)) for n in lens]
+        gen.set_context_limit(int(lens.max()) + args.new_tokens)
+    else:
+        lens = np.full(b, args.prompt_len)
+        gen.set_context_limit(args.prompt_len + args.new_tokens)  # positions cycle within it
+        rng = np.random.default_rng(args.seed * 1000 + rank)
+        prompts = rng.integers(0, cfg.vocab_size, size=(b, args.prompt_len))
+    torch.cuda.synchronize(device)
+    t_pf = time.perf_counter()
     gen.prefill(prompts)
+    torch.cuda.synchronize(device)
+    t_pf = time.perf_counter() - t_pf
     st = gen.state
-    first_pos = args.prompt_len
+    first_pos_d = torch.from_numpy(lens.astype(np.int32)).to(device)
 
     produced = 0  # tokens generated since the last position reset
 
     def step():
         nonlocal produced
         if produced == args.new_tokens:
-            st.positions.fill_(first_pos)
+            st.positions.copy_(first_pos_d)  # back to the end of each prompt: contexts stay within the cache
             produced = 0
         gen.step()
         produced += 1
@@ -582,7 +602,7 @@ def run_b200(args) -> None:
     h_, f_ = hcfg.hidden_size, hcfg.intermediate_size
     qkv_ = (hcfg.num_attention_heads + 2 * hcfg.num_key_value_heads) * hcfg.head_dim
     w_layer = (qkv_ * h_ + h_ * hcfg.num_attention_heads * hcfg.head_dim + 2 * f_ * h_ + h_ * f_) // 4
-    ctx_mean = args.prompt_len + (args.new_tokens + 1) / 2.0  # positions cycle prompt+1 .. prompt+new
+    ctx_mean = float(lens.mean()) + (args.new_tokens + 1) / 2.0  # positions cycle len+1 .. len+new (rank 0)
     kv_step = b * ctx_mean * 2 * hcfg.num_key_value_heads * hcfg.head_dim * 2 * hcfg.num_layers
     step_bytes = hcfg.num_layers * w_layer + 2 * hcfg.vocab_size * h_ + kv_step
     step_s = ms_max / args.steps / 1000.0
@@ -593,11 +613,18 @@ def run_b200(args) -> None:
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "int8xternary->int32 (bf16 act/KV, bf16 lm_head)",
+        "scaling": "strong" if c4 else "weak", "vs_baseline": None,
+        "dtype": "int8xternary->int32 (bf16 act/KV, bf16 lm_head)",
         "data": "synthetic (seeded random-init weights, uniform random prompt ids)",
-        "config": {"workload": "config2: batch-32 greedy decode, BitNet-2B-4T shape, 64-token prompts, "
-                               "128 new tokens, bf16 KV cache 2048, CUDA graph",
-                   "batch_per_gpu": b, "global_batch": b * world, "prompt_len": args.prompt_len,
+        "config": {"workload": (f"config4: {args.sequences} sequences split over {world} GPU(s), ragged contexts "
+                                f"U[128, 4096], {args.new_tokens} new tokens, bf16 KV cache {args.max_seq_len}, "
+                                "CUDA graph") if c4 else
+                               ("config2: batch-32 greedy decode, BitNet-2B-4T shape, 64-token prompts, "
+                                "128 new tokens, bf16 KV cache 2048, CUDA graph"),
+                   "batch_per_gpu": b, "global_batch": b * world,
+                   "prompt_len": (f"ragged, rank 0 mean {lens.mean():.0f}, max {lens.max()}" if c4
+                                  else args.prompt_len),
+                   "prefill_s_rank0": round(t_pf, 2),
                    "new_tokens": args.new_tokens, "layers": args.layers, "parallelism": f"dp{world} (batch split)",
                    "decode_path": args.decode_path,
                    "lm_head": f"vocab-sharded over {world} ranks (NCCL gathers)" if args.vocab_shard and world > 1
@@ -623,6 +650,14 @@ def run_b200(args) -> None:
 
 def main() -> None:
     args = parse()
+    c4 = args.workload == "config4"
+    if args.new_tokens is None:
+        args.new_tokens = 256 if c4 else 128
+    if args.max_seq_len is None:
+        args.max_seq_len = 4096 + args.new_tokens if c4 else 2048
+    if c4:
+        args.prefill_len = 0  # the prefill fills the ragged contexts; config 3 is measured in config2 runs
+        args.cpu_baseline_steps = 0
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
     if args.impl == "reference":
