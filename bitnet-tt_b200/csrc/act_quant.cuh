@@ -192,14 +192,15 @@ __device__ void aq_row_vec(const uint16_t* __restrict__ x, int M, int K, int ldx
     xr[c] = (valid && ch < KC8) ? reinterpret_cast<const uint4*>(x + (size_t)m * ldx)[ch] : make_uint4(0, 0, 0, 0);
   }
   if (has_gamma) {
-    double ss = 0.0;
+    double ssp[4] = {0.0, 0.0, 0.0, 0.0};  // four independent chains (exact in any order)
 #pragma unroll
     for (int c = 0; c < AQ_MAXC; ++c) {
       float f[8];
       aq_unpack8(xr[c], f);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) ss = fma((double)f[e], (double)f[e], ss);
+      for (int e = 0; e < 8; ++e) ssp[e & 3] = fma((double)f[e], (double)f[e], ssp[e & 3]);
     }
+    double ss = (ssp[0] + ssp[1]) + (ssp[2] + ssp[3]);
     ss = aq_allreduce<BAR>(ss, sc.d, OpAddD(), t);
     const float var = __double2float_rn(__ddiv_rn(ss, (double)K));
     const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
@@ -300,14 +301,15 @@ act_quant_warp_kernel(const uint16_t* __restrict__ x, int M, int K, int ldx, con
     xr[c] = (valid && ch < KC8) ? reinterpret_cast<const uint4*>(x + (size_t)m * ldx)[ch] : make_uint4(0, 0, 0, 0);
   }
   if (gamma != nullptr) {
-    double ss = 0.0;
+    double ssp[4] = {0.0, 0.0, 0.0, 0.0};  // four independent chains (exact in any order)
 #pragma unroll
     for (int c = 0; c < MAXC; ++c) {
       float f[8];
       aq_unpack8(xr[c], f);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) ss = fma((double)f[e], (double)f[e], ss);
+      for (int e = 0; e < 8; ++e) ssp[e & 3] = fma((double)f[e], (double)f[e], ssp[e & 3]);
     }
+    double ss = (ssp[0] + ssp[1]) + (ssp[2] + ssp[3]);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
     const float var = __double2float_rn(__ddiv_rn(ss, (double)K));
@@ -393,13 +395,14 @@ act_quant_warp_stream_kernel(const uint16_t* __restrict__ x, int M, int K, int l
   const uint4* grow = reinterpret_cast<const uint4*>(gamma);
   float r = 1.f;
   if (gamma != nullptr) {
-    double ss = 0.0;
+    double ssp[4] = {0.0, 0.0, 0.0, 0.0};  // four independent chains (exact in any order)
     for (int ch = lane; ch < KC8; ch += 32) {
       float f[8];
       aq_unpack8(valid ? xrow[ch] : make_uint4(0, 0, 0, 0), f);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) ss = fma((double)f[e], (double)f[e], ss);
+      for (int e = 0; e < 8; ++e) ssp[e & 3] = fma((double)f[e], (double)f[e], ssp[e & 3]);
     }
+    double ss = (ssp[0] + ssp[1]) + (ssp[2] + ssp[3]);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
     const float var = __double2float_rn(__ddiv_rn(ss, (double)K));

@@ -560,19 +560,34 @@ __global__ void __launch_bounds__(TC_THREADS, 2) bitlinear_tc_kernel(const TcPar
       const float wsc = seg_scale_of(p.seg, n);
       const bool row_ok = n < N;
       const int* rr = recv + row * ldr - m_begin;
-#pragma unroll 4
-      for (int m = m_begin + part; m < m_end; m += 2) {
-        const int mg = mt * T + m;
-        int a = -ctrl->rsum[m];
-        for (int j = 0; j < split; ++j) a += rr[j * 128 * ldr + m];
-        const float v = seg_uniform ? round_bf16(__fmul_rn((float)a, ctrl->fac0[m])) : scaled_bf16(a, wsc, ctrl->scale[m]);
-        if (row_ok && mg < p.M) {
-          const size_t o = (size_t)mg * N + n;
-          if (p.acc_out) p.acc_out[o] = a;
-          if (EPI == EPI_RESIDUAL_ADD)
-            p.y[o] = residual_add_bf16(p.residual[o], v);
-          else
-            p.y[o] = f32_to_bf16_bits(v);
+      // tokens in batches of 4 per thread; the batch's residuals are read before
+      // any of its stores (y may be the residual buffer, which keeps the
+      // compiler from moving a load above an earlier store)
+      for (int m0 = m_begin + part; m0 < m_end; m0 += 8) {
+        uint16_t res[4];
+        if (EPI == EPI_RESIDUAL_ADD) {
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int m = m0 + 2 * u, mg = mt * T + m;
+            res[u] = (m < m_end && row_ok && mg < p.M) ? p.residual[(size_t)mg * N + n] : (uint16_t)0;
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int m = m0 + 2 * u;
+          if (m >= m_end) break;
+          const int mg = mt * T + m;
+          int a = -ctrl->rsum[m];
+          for (int j = 0; j < split; ++j) a += rr[j * 128 * ldr + m];
+          const float v = seg_uniform ? round_bf16(__fmul_rn((float)a, ctrl->fac0[m])) : scaled_bf16(a, wsc, ctrl->scale[m]);
+          if (row_ok && mg < p.M) {
+            const size_t o = (size_t)mg * N + n;
+            if (p.acc_out) p.acc_out[o] = a;
+            if (EPI == EPI_RESIDUAL_ADD)
+              p.y[o] = residual_add_bf16(res[u], v);
+            else
+              p.y[o] = f32_to_bf16_bits(v);
+          }
         }
       }
     }
