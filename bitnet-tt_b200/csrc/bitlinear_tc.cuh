@@ -50,7 +50,7 @@ constexpr int TC_PRODUCER_WARP = 11;
 // sub-partition then admits only one CTA per SM)
 constexpr int TC_THREADS = 12 * 32;
 constexpr int TC_EPI_THREADS = TC_UNPACK_WARPS * 32;
-constexpr int TC_STAGE_CHUNKS = 4;  // 4 x 64 = 256 K positions per stage
+constexpr int TC_STAGE_CHUNKS = 4;  // 4 x 64 = 256 K positions per stage (the most; TcParams::sc)
 constexpr int TC_MAX_SLOTS = 16;
 constexpr int TC_MAX_NBUF = 8;      // A buffers in TMEM (64 columns each)
 constexpr int TC_TMEM_COLS = 512;       // one CTA per SM; 256 when two CTAs share an SM
@@ -72,9 +72,10 @@ struct TcParams {
   int split;
   int nbuf;  // A buffers in TMEM
   int tmem_cols;  // 512 (one CTA per SM) or 256 (two)
+  int sc;         // K chunks of 64 per stage: 4, or 2 for 256-token tiles (twice the stages in flight)
 };
 
-__host__ __device__ __forceinline__ int tc_slot_bytes(int T) { return TC_STAGE_CHUNKS * 2048 + TC_STAGE_CHUNKS * 64 * T; }
+__host__ __device__ __forceinline__ int tc_slot_bytes(int T, int sc = TC_STAGE_CHUNKS) { return sc * 2048 + sc * 64 * T; }
 // K split: rank j of the cluster owns tokens [j * tok_cap, (j + 1) * tok_cap);
 // one CTA's partial sums for one owner are 128 rows x ldr int32 (ldr odd, so
 // the owner's column reads are free of bank conflicts).
@@ -82,8 +83,9 @@ __host__ __device__ __forceinline__ int tc_tok_cap(int T, int split) { return (T
 __host__ __device__ __forceinline__ int tc_ldr(int T, int split) { return tc_tok_cap(T, split) | 1; }
 __host__ __device__ __forceinline__ int tc_part_bytes(int T, int split) { return 128 * tc_ldr(T, split) * 4; }
 __host__ __device__ __forceinline__ int tc_nacc(int T) { return T <= 32 ? 3 : (T <= 64 ? 2 : 1); }
-__host__ __device__ __forceinline__ int tc_nbuf(int T, int cols = TC_TMEM_COLS) {
-  const int nb = (cols - tc_nacc(T) * T) / 64;
+// A buffers of sc chunks (16 * sc TMEM columns each) beside the accumulators
+__host__ __device__ __forceinline__ int tc_nbuf(int T, int cols = TC_TMEM_COLS, int sc = TC_STAGE_CHUNKS) {
+  const int nb = (cols - tc_nacc(T) * T) / (16 * sc);
   return nb > TC_MAX_NBUF ? TC_MAX_NBUF : nb;
 }
 
@@ -117,16 +119,17 @@ __global__ void __launch_bounds__(TC_THREADS, 2) bitlinear_tc_kernel(const TcPar
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int nb = blockIdx.x, mt = blockIdx.y, ks = blockIdx.z;
-  const int T = p.T, KC = p.KC, nslot = p.nslot, split = p.split, NB = p.nbuf;
+  const int T = p.T, KC = p.KC, nslot = p.nslot, split = p.split, NB = p.nbuf, SC = p.sc;
   const int NACC = tc_nacc(T);
   const int kc_begin = (ks * KC) / split, kc_end = ((ks + 1) * KC) / split;
-  const int nstages = (kc_end - kc_begin + TC_STAGE_CHUNKS - 1) / TC_STAGE_CHUNKS;
+  const int nstages = (kc_end - kc_begin + SC - 1) / SC;
   // Every CTA of a launch reads the same activation block.  Starting each CTA
   // at a different K stage spreads those reads over the L2 instead of having
   // all SMs hit the same lines at once; the integer sum is order-independent.
   const int rot = nstages > 0 ? (int)((blockIdx.x + blockIdx.y * 7u) % (unsigned)nstages) : 0;
-  const int slot_bytes = tc_slot_bytes(T);
-  const int wslot_bytes = TC_STAGE_CHUNKS * 2048;
+  const int slot_bytes = tc_slot_bytes(T, SC);
+  const int wslot_bytes = SC * 2048;
+  const int acols = 16 * SC;  // TMEM columns of one A buffer
   const uint32_t ncols = (uint32_t)p.tmem_cols;
   volatile int* abort_flag = &ctrl->abort_flag;
 
@@ -160,15 +163,15 @@ __global__ void __launch_bounds__(TC_THREADS, 2) bitlinear_tc_kernel(const TcPar
   // prefetch while this one runs; it waits for this grid before reading it.
   pdl_trigger();
   const uint32_t tbase = ctrl->tmem_base;
-  const uint32_t tmem_d = tbase + NB * 64;  // D_i at tmem_d + i * T
+  const uint32_t tmem_d = tbase + NB * acols;  // D_i at tmem_d + i * T
 
   // logical stage s -> K chunks [kc0(s), kc0(s) + stage_chunks(s))
   auto kc0 = [&](int s) {
     int g = s + rot;
     if (g >= nstages) g -= nstages;
-    return kc_begin + g * TC_STAGE_CHUNKS;
+    return kc_begin + g * SC;
   };
-  auto stage_chunks = [&](int s) { return min(TC_STAGE_CHUNKS, kc_end - kc0(s)); };
+  auto stage_chunks = [&](int s) { return min(SC, kc_end - kc0(s)); };
   auto wait = [&](uint64_t* bar, uint32_t parity, int site) -> bool {
     if (*abort_flag) return false;
     if (!mbar_wait(bar, parity, site)) {
@@ -267,7 +270,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2) bitlinear_tc_kernel(const TcPar
         if (!wait_spin(&ctrl->a_full[b], (s / NB) & 1, 201)) break;
         if (!wait_spin(&ctrl->x_full[slot], (s / nslot) & 1, 207)) break;
         tc_fence_after();
-        const uint32_t a_base = tbase + b * 64;
+        const uint32_t a_base = tbase + b * acols;
         const uint32_t b_base = smem_u32(ring + (size_t)slot * slot_bytes + wslot_bytes);
         const int ksteps = 2 * stage_chunks(s);
         for (int kk = iss; kk < ksteps; kk += NACC) {
@@ -295,7 +298,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2) bitlinear_tc_kernel(const TcPar
       if (ok) ok = wait(&ctrl->w_full[slot], (s / nslot) & 1, 203);
       if (ok) {
         const uint8_t* wsm = ring + (size_t)slot * slot_bytes;
-        const uint32_t tst = tbase + ((uint32_t)(quarter * 32) << 16) + b * 64;
+        const uint32_t tst = tbase + ((uint32_t)(quarter * 32) << 16) + b * acols;
         const int nch = stage_chunks(s);
         for (int c = half; c < nch; c += 2) {
           const uint4 v = *reinterpret_cast<const uint4*>(wsm + c * 2048 + row * 16);

@@ -192,8 +192,8 @@ int dispatch_simt(const int8_t* q, const float* rs, const int32_t* rsum, int M, 
 // 512 columns, or two with 256.  Every resident CTA then gets its columns
 // immediately, so a CTA of a cluster can never sit in tcgen05.alloc while its
 // peers wait for it.
-size_t tc_smem_bytes(int T, int nslot, int split, int cols = TC_TMEM_COLS) {
-  const size_t ring = (size_t)nslot * tc_slot_bytes(T);
+size_t tc_smem_bytes(int T, int nslot, int split, int cols = TC_TMEM_COLS, int sc = TC_STAGE_CHUNKS) {
+  const size_t ring = (size_t)nslot * tc_slot_bytes(T, sc);
   const size_t stage = (size_t)T * TC_ST_LD * 2;  // staged bf16 output tile (no K split)
   const size_t recv = (size_t)2 * split * tc_part_bytes(T, split);  // receive slots + staging
   size_t bytes = TC_CTRL_BYTES + (split > 1 ? ring + recv : (ring > stage ? ring : stage));
@@ -202,13 +202,13 @@ size_t tc_smem_bytes(int T, int nslot, int split, int cols = TC_TMEM_COLS) {
 }
 size_t tc_smem_limit(int cols) { return cols == 512 ? kMaxDynSmem : (size_t)112 * 1024; }
 
-int tc_nslot(int T, int KC, int split, int cols = TC_TMEM_COLS) {
+int tc_nslot(int T, int KC, int split, int cols = TC_TMEM_COLS, int sc = TC_STAGE_CHUNKS) {
   const int chunks_max = (KC + split - 1) / split;
-  const int stages_max = (chunks_max + TC_STAGE_CHUNKS - 1) / TC_STAGE_CHUNKS;
+  const int stages_max = (chunks_max + sc - 1) / sc;
   int nslot = TC_MAX_SLOTS;
   if (nslot > stages_max) nslot = stages_max;
   if (nslot < 2) nslot = 2;
-  while (nslot > 2 && tc_smem_bytes(T, nslot, split, cols) > tc_smem_limit(cols)) --nslot;
+  while (nslot > 2 && tc_smem_bytes(T, nslot, split, cols, sc) > tc_smem_limit(cols)) --nslot;
   return nslot;
 }
 
@@ -239,20 +239,26 @@ int dispatch_tc(TcParams p, int ntile_n, int ntile_m, bitnet_stream_t st, const 
       if (split < 1) split = 1;
     }
   }
+  // K chunks per stage.  Halving the stage for 256-token tiles (twice the
+  // stages in flight) was measured slower: a stage's copies cost ~0.7 us of
+  // fixed time whatever their size, so fewer, larger stages win.
+  const int sc = TC_STAGE_CHUNKS;
   int cols = TC_TMEM_COLS;
   // two CTAs per SM, when both the tensor memory and the shared memory of the
   // smallest ring fit twice
-  if ((long)tiles * split > dev.sms && tc_nbuf(p.T, 256) >= 2 && tc_smem_bytes(p.T, 2, split, 256) <= tc_smem_limit(256))
+  if ((long)tiles * split > dev.sms && tc_nbuf(p.T, 256, sc) >= 2 &&
+      tc_smem_bytes(p.T, 2, split, 256, sc) <= tc_smem_limit(256))
     cols = 256;
   if (split > 8 || split > p.KC) return BITNET_ERR_INVALID_ARGUMENT;
   if (split > 1 && p.T > 64) return BITNET_ERR_INVALID_ARGUMENT;
-  const int nslot = tc_nslot(p.T, p.KC, split, cols);
-  const size_t smem = tc_smem_bytes(p.T, nslot, split, cols);
+  const int nslot = tc_nslot(p.T, p.KC, split, cols, sc);
+  const size_t smem = tc_smem_bytes(p.T, nslot, split, cols, sc);
   if (smem > tc_smem_limit(cols)) return BITNET_ERR_INVALID_ARGUMENT;
   p.nslot = nslot;
   p.split = split;
   p.tmem_cols = cols;
-  p.nbuf = tc_nbuf(p.T, cols);
+  p.nbuf = tc_nbuf(p.T, cols, sc);
+  p.sc = sc;
   return launch(k, dim3(ntile_n, ntile_m, split), dim3(TC_THREADS), smem, st, split, p);
 }
 
