@@ -49,12 +49,12 @@ FALLBACK_BF16_TFLOPS = 1590.0
 # captured launch); profiles/decode_step_dram_bytes_b32.md has the capture.
 # None where no capture of the current kernel exists.
 NCU_TRAFFIC_BYTES: dict[str, float | None] = {
-    "bitlinear_qkv": 2588928.0,
-    "bitlinear_o": 1934848.0,
-    "bitlinear_gate_up": 8984832.0,
-    "bitlinear_down": 4858368.0,
+    "bitlinear_qkv": 2610688.0,
+    "bitlinear_o": 1955840.0,
+    "bitlinear_gate_up": 9004800.0,
+    "bitlinear_down": 4880384.0,
     "act_quant": 192512.0,
-    "lm_head": 660284928.0,
+    "lm_head": 659942144.0,
 }
 
 # Kernel classes timed by kernel_rooflines, grouped by the kernel (template
