@@ -24,6 +24,7 @@ __device__ __forceinline__ uint4 ldg_stream16(const void* p) {
 
 constexpr int SIMT_THREADS = 256;
 constexpr int SIMT_MAX_M = 8;
+constexpr int SIMT_REG_CHUNKS = 16;  // 64-wide K chunks a lane holds in registers at once (16 B each)
 
 // grid.x = ceil(N / rows_per_cta).  dynamic smem = Kp * 8 (q rows 0..7) + reduction.
 template <int EPI, int MT>
@@ -47,15 +48,26 @@ bitlinear_simt_kernel(const int8_t* __restrict__ q, const float* __restrict__ ro
   const int kc_begin = (ks * KC) / KS, kc_end = ((ks + 1) * KC) / KS;
 
   const uint8_t* wrow = w + wlayout_offset(n, 0, KC);
+  const int nch = kc_end - kc_begin;
 
+  // The lane's weight chunks (up to SIMT_REG_CHUNKS at once) are loaded before
+  // griddepcontrol.wait: the weights do not come from the previous kernel, so
+  // their HBM reads overlap it; only the activation codes wait.
+  uint4 wv[SIMT_REG_CHUNKS];
+  auto load_w = [&](int b0) {
+#pragma unroll
+    for (int u = 0; u < SIMT_REG_CHUNKS; ++u)
+      wv[u] = (b0 + u < nch) ? ldg_stream16(wrow + (size_t)(kc_begin + b0 + u) * 2048u) : make_uint4(0, 0, 0, 0);
+  };
   pdl_trigger();  // the next kernel may launch; it waits for this grid before reading
+  load_w(0);
   pdl_wait();
-  // Stage q rows 0..7 of the (single) token tile: for each 16-wide K chunk the
-  // first core matrix (8 rows x 16 B) of the tile.
+  // Stage the tile's q rows 0..MT-1: for each 16-wide K chunk the first rows of
+  // its first core matrix (8 rows x 16 B).
   const int C16 = Kp >> 4;
-  for (int i = tid; i < C16 * 8; i += SIMT_THREADS) {
-    const int c = i >> 3, r = i & 7;
-    sq[i] = *reinterpret_cast<const uint4*>(q + ((size_t)c * (T >> 3)) * 128u + (size_t)r * 16u);
+  for (int i = tid; i < C16 * MT; i += SIMT_THREADS) {
+    const int c = i / MT, r = i % MT;
+    sq[c * 8 + r] = *reinterpret_cast<const uint4*>(q + ((size_t)c * (T >> 3)) * 128u + (size_t)r * 16u);
   }
   __syncthreads();
 
@@ -63,15 +75,12 @@ bitlinear_simt_kernel(const int8_t* __restrict__ q, const float* __restrict__ ro
 #pragma unroll
   for (int m = 0; m < MT; ++m) acc[m] = 0;
 
-  // Four 16-byte weight loads in flight per lane before any of them is consumed.
-  for (int kc0 = kc_begin; kc0 < kc_end; kc0 += 4) {
-    uint4 wv[4];
+  for (int b0 = 0; b0 < nch; b0 += SIMT_REG_CHUNKS) {
+    if (b0 > 0) load_w(b0);
+    const int kc0 = kc_begin + b0;
 #pragma unroll
-    for (int u = 0; u < 4; ++u)
-      wv[u] = (kc0 + u < kc_end) ? ldg_stream16(wrow + (size_t)(kc0 + u) * 2048u) : make_uint4(0, 0, 0, 0);
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      if (kc0 + u >= kc_end) break;
+    for (int u = 0; u < SIMT_REG_CHUNKS; ++u) {
+      if (b0 + u >= nch) break;
       const uint32_t xw[4] = {wv[u].x, wv[u].y, wv[u].z, wv[u].w};
 #pragma unroll
       for (int wi = 0; wi < 4; ++wi) {
