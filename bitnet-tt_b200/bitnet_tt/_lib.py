@@ -313,6 +313,24 @@ def bitlinear_q(bufs: ActBuffers, m: int, k: int, w_packed: torch.Tensor, n: int
           "bitnet_bitlinear_q")
 
 
+SIMT_FUSED_MAX_M = 4  # bitnet_bitlinear runs as one fused launch for M <= this (the CUDA-core path)
+
+
+def bitlinear_fused(x: torch.Tensor, gamma: torch.Tensor | None, eps: float, bufs: ActBuffers, w_packed: torch.Tensor,
+                    n: int, segments: Segments | None, epilogue: int, residual: torch.Tensor | None, y: torch.Tensor,
+                    acc_out: torch.Tensor | None = None, path: int = PATH_AUTO) -> None:
+    """bitnet_bitlinear: RMSNorm + act-quant + ternary contraction + epilogue.  For
+    M <= SIMT_FUSED_MAX_M one kernel; otherwise the act-quant and BitLinear
+    launches (bufs holds the codes)."""
+    m, k = x.shape
+    if x.dtype != torch.bfloat16 or x.stride(0) != k:
+        raise ValueError("x must be contiguous bf16 [M, K]")
+    seg = ctypes.byref(segments) if segments is not None else None
+    check(load().bitnet_bitlinear(ptr(x), m, k, ptr(gamma), float(eps), ptr(w_packed), n, seg, epilogue,
+                                  ptr(residual), ptr(y), ptr(acc_out), ptr(bufs.q), ptr(bufs.row_scale),
+                                  ptr(bufs.row_sum), path, stream_handle()), "bitnet_bitlinear")
+
+
 def gqa_decode_workspace_bytes(b: int, n_heads: int, n_kv: int, max_ctx: int) -> int:
     return int(load().bitnet_gqa_decode_workspace_bytes(b, n_heads, n_kv, max_ctx))
 

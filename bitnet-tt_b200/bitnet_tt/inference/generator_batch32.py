@@ -137,7 +137,10 @@ class Batch32Generator:
         self._graph: torch.cuda.CUDAGraph | None = None
         # persistent=True: every layer in one launch (batch <= 32); default: 9 launches per layer
         self.persistent = bool(persistent) and batch_size <= PADDED_BATCH
-        self.launches_per_step = 6 if self.persistent else 9 * self.config.num_layers + 5
+        nl = self.config.num_layers
+        # per layer: 4 fused BitLinear calls (1 launch each up to SIMT_FUSED_MAX_M tokens, else 2) + attention
+        per_layer = 5 if batch_size <= _lib.SIMT_FUSED_MAX_M else 9
+        self.launches_per_step = 6 if self.persistent else per_layer * nl + 5
         # vocab_shard_group: a torch.distributed group over which the lm_head is
         # split by vocabulary rows (batch-split multi-GPU decoding); its gathers
         # run outside the captured graph, after each replay
@@ -195,18 +198,19 @@ class Batch32Generator:
                 st.plan = _lib.DecodePlan(m, st.hidden, st.qkv, st.attn, st.mid, st.positions, st.rope_cos,
                                           st.rope_sin, st.caches, st.max_ctx, st.attn_ws)
             st.plan.run()
+        # per layer: fused norm + act-quant + BitLinear calls (one launch each
+        # below the ridge batch, act-quant + BitLinear above it) and the attention
         for layer, cache in zip(m.layers, st.caches) if not self.persistent else ():
             attn = layer.self_attn
-            _lib.act_quant(st.hidden, layer.input_layernorm.weight, eps, st.act_h)
-            attn.qkv_proj.forward_into(st.act_h, b, st.qkv)
+            attn.qkv_proj.forward_fused(st.hidden, layer.input_layernorm.weight, eps, st.act_h, st.qkv)
             attn.decode_attention(st.qkv, st.positions, st.rope_cos, st.rope_sin, cache, st.attn, st.max_ctx,
                                   st.attn_ws)
-            _lib.act_quant(st.attn, attn.attn_sub_norm.weight, eps, st.act_h)
-            attn.o_proj.forward_into(st.act_h, b, st.hidden, residual=st.hidden)
-            _lib.act_quant(st.hidden, layer.post_attention_layernorm.weight, eps, st.act_h)
-            layer.mlp.gate_up_proj.forward_into(st.act_h, b, st.mid)
-            _lib.act_quant(st.mid, layer.mlp.ffn_sub_norm.weight, eps, st.act_f)
-            layer.mlp.down_proj.forward_into(st.act_f, b, st.hidden, residual=st.hidden)
+            attn.o_proj.forward_fused(st.attn, attn.attn_sub_norm.weight, eps, st.act_h, st.hidden,
+                                      residual=st.hidden)
+            layer.mlp.gate_up_proj.forward_fused(st.hidden, layer.post_attention_layernorm.weight, eps, st.act_h,
+                                                 st.mid)
+            layer.mlp.down_proj.forward_fused(st.mid, layer.mlp.ffn_sub_norm.weight, eps, st.act_f, st.hidden,
+                                              residual=st.hidden)
         _lib.rmsnorm(st.hidden, m.norm.weight, eps, st.normed)
         if self.vocab_head is None:
             m.lm_head_argmax(st.normed, st.argmax_ws, st.ids, st.logits, st.positions)

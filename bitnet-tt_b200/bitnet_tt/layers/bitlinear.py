@@ -130,6 +130,14 @@ class Linear:
         _lib.bitlinear_q(bufs, m, self.in_features, self.weight, self.out_features, self.segments(), epi,
                          residual, y, acc_out=acc_out, path=path)
 
+    def forward_fused(self, x: torch.Tensor, norm_weight: torch.Tensor | None, eps: float, bufs: _lib.ActBuffers,
+                      y: torch.Tensor, residual: torch.Tensor | None = None) -> None:
+        """Norm + act-quant + contraction from bf16 rows x [M, in] (bitnet_bitlinear:
+        one launch below the ridge batch, two above; `bufs` holds the codes)."""
+        epi = self.epilogue if residual is None else _lib.EPI_RESIDUAL_ADD
+        _lib.bitlinear_fused(x, norm_weight, eps, bufs, self.weight, self.out_features, self.segments(), epi,
+                             residual, y)
+
     def __call__(self, x: torch.Tensor, norm_weight: torch.Tensor | None = None,
                  norm_epsilon: float | None = None, residual: torch.Tensor | None = None) -> torch.Tensor:
         if self.weight is None:

@@ -9,6 +9,7 @@
 // The quantised activation rows (at most 8) sit in shared memory and are read
 // as warp-wide broadcasts.
 #pragma once
+#include "act_quant.cuh"
 #include "common.cuh"
 #include "epilogue.cuh"
 
@@ -26,19 +27,34 @@ constexpr int SIMT_THREADS = 256;
 constexpr int SIMT_MAX_M = 8;
 constexpr int SIMT_REG_CHUNKS = 16;  // 64-wide K chunks a lane holds in registers at once (16 B each)
 
+// Fused mode: the CTA computes the RMSNorm + int8 act-quant of the (at most 8)
+// token rows itself, straight into its shared-memory code tile, instead of
+// reading codes that a separate act-quant launch wrote.  x == nullptr: off.
+struct SimtFuse {
+  const uint16_t* x;  // bf16 [M, ldx], rows 16-byte aligned
+  int ldx, K;
+  const uint16_t* gamma;  // nullable
+  float eps;
+};
+
 // grid.x = ceil(N / rows_per_cta).  dynamic smem = Kp * 8 (q rows 0..7) + reduction.
 template <int EPI, int MT>
-__global__ void __launch_bounds__(SIMT_THREADS)
+__global__ void __launch_bounds__(SIMT_THREADS, 2)
 bitlinear_simt_kernel(const int8_t* __restrict__ q, const float* __restrict__ row_scale,
                       const int32_t* __restrict__ row_sum, int M, int Kp, int T, const uint8_t* __restrict__ w,
                       int N, bitnet_segments_dev seg, const uint16_t* residual, uint16_t* y,
-                      int32_t* __restrict__ acc_out) {
+                      int32_t* __restrict__ acc_out, const SimtFuse fz) {
   constexpr int RG = (EPI == EPI_RELU2_MUL) ? 2 : 1;  // 32-row groups per CTA
   constexpr int KS = 8 / RG;                          // K splits per row group
   extern __shared__ __align__(16) uint8_t smem_simt[];
   uint8_t* smem = smem_simt;
   uint4* sq = reinterpret_cast<uint4*>(smem);                     // [Kp/16][8 rows] x 16 B
   int* sred = reinterpret_cast<int*>(smem + (size_t)Kp * 8);      // [8 warps][MT][32]
+  __shared__ float s_scale[SIMT_MAX_M];  // fused mode: per-token scale and code sum
+  __shared__ int s_sum[SIMT_MAX_M];
+  __shared__ double s_rd[AQ_THREADS / 32];
+  __shared__ float s_rf[AQ_THREADS / 32];
+  __shared__ int s_ri[AQ_THREADS / 32];
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int rg = warp / KS, ks = warp % KS;
@@ -61,13 +77,25 @@ bitlinear_simt_kernel(const int8_t* __restrict__ q, const float* __restrict__ ro
   };
   pdl_trigger();  // the next kernel may launch; it waits for this grid before reading
   load_w(0);
+  const bool fused = fz.x != nullptr;
+  uint4 gr[AQ_MAXC];
+  if (fused) aq_load_gamma(gr, fz.gamma, fz.K, tid);  // gamma does not come from the previous kernel either
   pdl_wait();
-  // Stage the tile's q rows 0..MT-1: for each 16-wide K chunk the first rows of
-  // its first core matrix (8 rows x 16 B).
-  const int C16 = Kp >> 4;
-  for (int i = tid; i < C16 * MT; i += SIMT_THREADS) {
-    const int c = i / MT, r = i % MT;
-    sq[c * 8 + r] = *reinterpret_cast<const uint4*>(q + ((size_t)c * (T >> 3)) * 128u + (size_t)r * 16u);
+  if (fused) {
+    // sq is the code layout of a token tile of 8 rows: for each 16-wide K chunk
+    // 8 rows x 16 B, i.e. the act-quant layout with T = 8
+    const AqScratch sc{s_rd, s_rf, s_ri};
+    for (int m = 0; m < M; ++m)
+      aq_row_vec<0>(fz.x, M, fz.K, fz.ldx, fz.gamma != nullptr, gr, fz.eps, reinterpret_cast<int8_t*>(sq), s_scale,
+                    s_sum, nullptr, 8, Kp, m, sc, tid);
+  } else {
+    // Stage the tile's q rows 0..MT-1: for each 16-wide K chunk the first rows of
+    // its first core matrix (8 rows x 16 B).
+    const int C16 = Kp >> 4;
+    for (int i = tid; i < C16 * MT; i += SIMT_THREADS) {
+      const int c = i / MT, r = i % MT;
+      sq[c * 8 + r] = *reinterpret_cast<const uint4*>(q + ((size_t)c * (T >> 3)) * 128u + (size_t)r * 16u);
+    }
   }
   __syncthreads();
 
@@ -120,13 +148,14 @@ bitlinear_simt_kernel(const int8_t* __restrict__ q, const float* __restrict__ ro
         ag += sred[((0 * KS + s) * MT + m) * 32 + p];
         au += sred[((1 * KS + s) * MT + m) * 32 + p];
       }
-      ag -= row_sum[m];
-      au -= row_sum[m];
+      const int rsm = fused ? s_sum[m] : row_sum[m];
+      ag -= rsm;
+      au -= rsm;
       if (acc_out) {
         acc_out[(size_t)m * N + ng] = ag;
         acc_out[(size_t)m * N + nu] = au;
       }
-      const float sm = row_scale[m];
+      const float sm = fused ? s_scale[m] : row_scale[m];
       const float g = scaled_bf16(ag, seg.scale[0], sm);
       const float u = scaled_bf16(au, seg.scale[1], sm);
       const int o = (n0 >> 6) * 32 + p;
@@ -141,9 +170,9 @@ bitlinear_simt_kernel(const int8_t* __restrict__ q, const float* __restrict__ ro
       int a = 0;
 #pragma unroll
       for (int s = 0; s < KS; ++s) a += sred[(s * MT + m) * 32 + r];
-      a -= row_sum[m];
+      a -= fused ? s_sum[m] : row_sum[m];
       if (acc_out) acc_out[(size_t)m * N + nn] = a;
-      const float v = scaled_bf16(a, seg_scale_of(seg, nn), row_scale[m]);
+      const float v = scaled_bf16(a, seg_scale_of(seg, nn), fused ? s_scale[m] : row_scale[m]);
       const size_t o = (size_t)m * N + nn;
       if (EPI == EPI_RESIDUAL_ADD)
         y[o] = residual_add_bf16(residual[o], v);

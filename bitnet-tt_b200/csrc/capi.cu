@@ -166,24 +166,24 @@ size_t lm_head_part_bytes(int B, int grid) { return (size_t)grid * B * sizeof(Ar
 template <int EPI, int MT>
 int launch_simt(const int8_t* q, const float* rs, const int32_t* rsum, int M, int Kp, int T, const uint8_t* w,
                 int N, const bitnet_segments_dev& seg, const uint16_t* res, uint16_t* y, int32_t* acc,
-                bitnet_stream_t st, int mt_idx) {
+                bitnet_stream_t st, int mt_idx, const SimtFuse& fz) {
   auto k = bitlinear_simt_kernel<EPI, MT>;
   if (int e = ensure_smem(k, &g_smem_simt[EPI][mt_idx])) return e;
   const int rows = 32 * (EPI == EPI_RELU2_MUL ? 2 : 1);
   const size_t smem = (size_t)Kp * 8 + (size_t)8 * MT * 32 * 4;
   if (smem > kMaxDynSmem) return BITNET_ERR_INVALID_ARGUMENT;
   return launch(k, dim3((N + rows - 1) / rows), dim3(SIMT_THREADS), smem, st, 1, q, rs, rsum, M, Kp, T, w, N, seg,
-                res, y, acc);
+                res, y, acc, fz);
 }
 
 template <int EPI>
 int dispatch_simt(const int8_t* q, const float* rs, const int32_t* rsum, int M, int Kp, int T, const uint8_t* w,
                   int N, const bitnet_segments_dev& seg, const uint16_t* res, uint16_t* y, int32_t* acc,
-                  bitnet_stream_t st) {
-  if (M <= 1) return launch_simt<EPI, 1>(q, rs, rsum, M, Kp, T, w, N, seg, res, y, acc, st, 0);
-  if (M <= 2) return launch_simt<EPI, 2>(q, rs, rsum, M, Kp, T, w, N, seg, res, y, acc, st, 1);
-  if (M <= 4) return launch_simt<EPI, 4>(q, rs, rsum, M, Kp, T, w, N, seg, res, y, acc, st, 2);
-  return launch_simt<EPI, 8>(q, rs, rsum, M, Kp, T, w, N, seg, res, y, acc, st, 3);
+                  bitnet_stream_t st, const SimtFuse& fz = SimtFuse{nullptr, 0, 0, nullptr, 0.f}) {
+  if (M <= 1) return launch_simt<EPI, 1>(q, rs, rsum, M, Kp, T, w, N, seg, res, y, acc, st, 0, fz);
+  if (M <= 2) return launch_simt<EPI, 2>(q, rs, rsum, M, Kp, T, w, N, seg, res, y, acc, st, 1, fz);
+  if (M <= 4) return launch_simt<EPI, 4>(q, rs, rsum, M, Kp, T, w, N, seg, res, y, acc, st, 2, fz);
+  return launch_simt<EPI, 8>(q, rs, rsum, M, Kp, T, w, N, seg, res, y, acc, st, 3, fz);
 }
 
 // Shared-memory request of the tcgen05 BitLinear.  Besides the ring and the
@@ -444,6 +444,34 @@ int bitnet_bitlinear(const void* x, int M, int K, const void* gamma, float eps, 
                      const bitnet_segments_t* segments, int epilogue, const void* residual, void* y, int32_t* acc_out,
                      int8_t* q_ws, float* scale_ws, int32_t* sum_ws, int path, bitnet_stream_t stream) {
   if (!q_ws || !scale_ws || !sum_ws) return BITNET_ERR_INVALID_ARGUMENT;
+  // Below the ridge (the CUDA-core path) one launch does everything: each CTA
+  // normalises and quantises the few token rows itself (same codes as
+  // bitnet_act_quant), so no act-quant launch and no code buffer round trip.
+  const int path_r = path == BITNET_PATH_AUTO ? ((M <= g_simt_max_m.load()) ? BITNET_PATH_SIMT : BITNET_PATH_TCGEN05)
+                                              : path;
+  const int Kp = round_up(K, 64);
+  if (path_r == BITNET_PATH_SIMT && x && M > 0 && M <= SIMT_MAX_M && K > 0 && K % 8 == 0 &&
+      Kp <= 8 * AQ_THREADS * AQ_MAXC && aligned(x, 16) && (!gamma || aligned(gamma, 16)) && eps >= 0.f) {
+    DevInfo* d;
+    if (int e = device_info(&d)) return e;
+    if (!w_packed || !y || N <= 0) return BITNET_ERR_INVALID_ARGUMENT;
+    if (epilogue < BITNET_EPI_NONE || epilogue > BITNET_EPI_RESIDUAL_ADD) return BITNET_ERR_INVALID_ARGUMENT;
+    if (epilogue == BITNET_EPI_RESIDUAL_ADD && !residual) return BITNET_ERR_INVALID_ARGUMENT;
+    if (epilogue == BITNET_EPI_RELU2_MUL && (N % 64) != 0) return BITNET_ERR_INVALID_ARGUMENT;
+    if (!aligned(w_packed, 16) || !aligned(y, 2) || (residual && !aligned(residual, 2)) || (acc_out && !aligned(acc_out, 4)))
+      return BITNET_ERR_ALIGNMENT;
+    bitnet_segments_dev seg;
+    if (int e = to_dev_segments(segments, N, epilogue, &seg)) return e;
+    const SimtFuse fz{(const uint16_t*)x, K, K, (const uint16_t*)gamma, eps};
+    const uint16_t* res = (const uint16_t*)residual;
+    uint16_t* yy = (uint16_t*)y;
+    const int T = act_tile_of(M);
+    switch (epilogue) {
+      case BITNET_EPI_NONE: return dispatch_simt<EPI_NONE>(nullptr, nullptr, nullptr, M, Kp, T, w_packed, N, seg, res, yy, acc_out, stream, fz);
+      case BITNET_EPI_RELU2_MUL: return dispatch_simt<EPI_RELU2_MUL>(nullptr, nullptr, nullptr, M, Kp, T, w_packed, N, seg, res, yy, acc_out, stream, fz);
+      default: return dispatch_simt<EPI_RESIDUAL_ADD>(nullptr, nullptr, nullptr, M, Kp, T, w_packed, N, seg, res, yy, acc_out, stream, fz);
+    }
+  }
   if (int e = bitnet_act_quant(x, M, K, K, gamma, eps, q_ws, scale_ws, sum_ws, nullptr, stream)) return e;
   return bitnet_bitlinear_q(q_ws, scale_ws, sum_ws, M, K, w_packed, N, segments, epilogue, residual, y, acc_out,
                             path, stream);

@@ -215,3 +215,35 @@ def test_bitlinear_rejects_bad_arguments(cuda):
         L.bitlinear_q(bufs, 9, 64, w, 128, None, L.EPI_NONE, None, y, path=L.PATH_SIMT)  # SIMT serves M <= 8
     with pytest.raises(RuntimeError, match="invalid argument"):
         L.bitlinear_q(bufs, 4, 64, w, 128, L.Segments.make([100], [1.0]), L.EPI_NONE, None, y)  # seg end != N
+
+
+@pytest.mark.parametrize("m", [1, 2, 3, 4])
+@pytest.mark.parametrize("epilogue", ["none", "relu2_mul", "residual_add"])
+@pytest.mark.parametrize("k", [2560, 6912])
+def test_fused_bitlinear_small_m_equals_two_launches(cuda, m, epilogue, k):
+    """bitnet_bitlinear below the ridge batch: one kernel that normalises and
+    quantises the token rows itself, bit-identical to act-quant + BitLinear."""
+    L = _lib()
+    n = 1024
+    x = rand_bf16((m, k), seed=m * 10 + k).to(cuda)
+    gamma = (1 + 0.1 * rand_bf16((k,), seed=k + 1).float()).to(torch.bfloat16).to(cuda)
+    w = rand_ternary(n, k, seed=n + k)
+    wp = L.pack_ternary(torch.from_numpy(w).to(cuda))
+    epi = {"none": L.EPI_NONE, "relu2_mul": L.EPI_RELU2_MUL, "residual_add": L.EPI_RESIDUAL_ADD}[epilogue]
+    seg = L.Segments.make([n // 2, n], [0.021, 0.017]) if epilogue == "relu2_mul" else L.Segments.make([n], [0.02])
+    nout = n // 2 if epilogue == "relu2_mul" else n
+    res = rand_bf16((m, nout), seed=5).to(cuda) if epilogue == "residual_add" else None
+    ref_bufs = L.ActBuffers(m, k, cuda)
+    L.act_quant(x, gamma, 1e-5, ref_bufs)
+    y_ref = torch.empty((m, nout), dtype=torch.bfloat16, device=cuda)
+    acc_ref = torch.empty((m, n), dtype=torch.int32, device=cuda)
+    L.bitlinear_q(ref_bufs, m, k, wp, n, seg, epi, res, y_ref, acc_out=acc_ref, path=L.PATH_SIMT)
+    bufs = L.ActBuffers(m, k, cuda)
+    for _ in range(2):
+        y = torch.zeros_like(y_ref)
+        acc = torch.zeros_like(acc_ref)
+        L.bitlinear_fused(x, gamma, 1e-5, bufs, wp, n, seg, epi, res, y, acc_out=acc)
+        torch.cuda.synchronize()
+        assert L.last_device_status()[0] == 0
+        assert torch.equal(acc, acc_ref)
+        assert torch.equal(y, y_ref)
