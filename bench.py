@@ -232,24 +232,25 @@ def model_config(args):
 # ---------------------------------------------------------------------------
 # CPU side: the oracle (restatement of the reference's CPU path)
 # ---------------------------------------------------------------------------
-def cpu_decode_sample(args, steps: int, budget_s: float | None = None) -> dict:
+def cpu_decode_sample(args, steps: int, budget_s: float | None = None, warm: int = 1) -> dict:
     """Build the CPU oracle of the same model and time `steps` batch decode steps
-    (1 untimed warm step first) at the prompt's context."""
+    (`warm` untimed steps first) at the prompt's context."""
     from bitnet_tt.utils.weights import synthetic_state_dict
     from oracle.model import OracleBitNet
 
     torch.set_num_threads(os.cpu_count() or 1)
     cfg = model_config(args)
     sd = synthetic_state_dict(cfg, args.seed, device="cpu")
-    ctx = args.prompt_len + args.new_tokens + 2
+    ctx = args.prompt_len + args.new_tokens + max(1, warm) + 1
     o = OracleBitNet(cfg, sd, max_len=ctx, quant="torch")
     b = args.batch
     caches = o.new_cache(b)
     rng = np.random.default_rng(args.seed)
     ids = torch.from_numpy(rng.integers(0, cfg.vocab_size, size=b).astype(np.int32))
     pos = torch.full((b,), args.prompt_len, dtype=torch.int32)
-    ids, _ = o.step(ids, pos, caches)  # warm
-    pos = pos + 1
+    for _ in range(max(1, warm)):  # untimed
+        ids, _ = o.step(ids, pos, caches)
+        pos = pos + 1
     done, t0 = 0, time.perf_counter()
     while done < steps:
         ids, _ = o.step(ids, pos, caches)
@@ -266,16 +267,24 @@ def run_reference(args) -> None:
     if rank != 0:
         return
     want = max(1, args.steps)
-    r = cpu_decode_sample(args, want, budget_s=args.ref_budget_s)
+    # the timed steps stop after --ref-budget-s seconds of CPU work (each step is ~1 s on 16 threads)
+    r = cpu_decode_sample(args, want, budget_s=args.ref_budget_s, warm=args.warmup)
     sample = (f"{r['steps']} of {want} requested batch-{args.batch} decode steps of the full "
-              f"{args.layers}-layer model (context {args.prompt_len + 1}..), CPU oracle, {r['threads']} threads")
+              f"{args.layers}-layer model (context {args.prompt_len + args.warmup}..), CPU oracle, "
+              f"{r['threads']} threads, after {args.warmup} untimed steps")
+    c1 = args.workload == "config1"
     line = {
-        "impl": "reference", "metric": METRIC, "value": r["tok_s"], "unit": "tok/s", "n_gpus": world,
-        "steps": r["steps"], "warmup": 1, "ms_per_step": 1000.0 * r["seconds"] / r["steps"],
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8xternary->int32",
-        "data": "synthetic",
-        "config": {"workload": "config2: batch-32 greedy decode, 64-token random prompts, bf16 KV",
-                   "batch": args.batch, "prompt_len": args.prompt_len, "layers": args.layers},
+        "impl": "reference", "metric": METRIC_C1 if c1 else METRIC, "value": r["tok_s"], "unit": "tok/s",
+        "n_gpus": world, "steps": r["steps"], "warmup": args.warmup, "ms_per_step": 1000.0 * r["seconds"] / r["steps"],
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int8xternary->int32 (bf16 act/KV, bf16 lm_head)",
+        "data": "synthetic (seeded random-init weights, uniform random prompt ids)",
+        "config": {"workload": ("config1: batch-1 greedy decode, BitNet-2B-4T shape, 16-token prompt, 128 new "
+                                "tokens") if c1 else
+                               ("config2: batch-32 greedy decode, BitNet-2B-4T shape, 64-token prompts, "
+                                "128 new tokens, bf16 KV cache 2048"),
+                   "batch_per_gpu": args.batch, "global_batch": args.batch, "prompt_len": args.prompt_len,
+                   "new_tokens": args.new_tokens, "layers": args.layers, "parallelism": "CPU oracle, rank 0"},
         "cpu_baseline": {"value": r["tok_s"], "unit": "tok/s", "cores": r["threads"], "kind": "port",
                          "sample": sample},
         "e2e": {"value": r["tok_s"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
