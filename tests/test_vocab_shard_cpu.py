@@ -9,6 +9,7 @@ before the gather, and a shape the head rejects before any collective.
 from __future__ import annotations
 
 import datetime
+import time
 import multiprocessing as mp
 import os
 import socket
@@ -92,10 +93,28 @@ def _worker(rank: int, world: int, port: int, mode: str, q) -> None:
         if mode == "rank_fails" and rank == 1:
             q.put((rank, "raised"))
             raise SystemExit(3)  # leaves before the gather
+        if mode == "stalls" and rank == 1:
+            q.put((rank, ("stalled", time.time())))
+            time.sleep(12)  # never reaches the gather in time; the peer's gather must end with an error
+            return
+        if mode == "fails_after":
+            head.step(h, ids, pos)  # one complete step on both ranks
+            if rank == 1:
+                q.put((rank, "raised after a step"))
+                raise SystemExit(3)
+            t0 = time.time()
+            try:
+                head.step(h, ids, pos)
+                q.put((rank, "no error"))
+            except Exception as e:  # noqa: BLE001 - the failure mode under test
+                q.put((rank, (f"error: {type(e).__name__}", time.time() - t0)))
+            return
         try:
+            t0 = time.time()
             head.step(h, ids, pos)
         except Exception as e:  # noqa: BLE001 - the failure mode under test
-            q.put((rank, f"error: {type(e).__name__}"))
+            q.put((rank, f"error: {type(e).__name__}" if mode != "stalls" else
+                   (f"error: {type(e).__name__}", time.time())))
             return
         logits = (h.float() @ w.t()).to(torch.bfloat16).float()
         ref = (logits == logits.max(dim=1).values[:, None]).int().argmax(dim=1).to(torch.int32)
@@ -167,3 +186,21 @@ def test_vocab_shard_rank_failure_is_an_error_not_a_hang():
 def test_vocab_shard_rejects_wrong_hidden_width():
     out = _run("shape")
     assert out[0] == "ValueError" and out[1] == "ValueError"
+
+
+def test_vocab_shard_rank_failure_after_a_step_is_an_error_not_a_hang():
+    out = _run("fails_after")
+    assert out[1] == "raised after a step"
+    msg, waited = out[0]
+    assert msg.startswith("error"), msg
+    assert waited < 30.0  # the process-group timeout (5 s), not a hang
+
+
+def test_vocab_shard_stalled_peer_times_out_with_an_error():
+    """A rank that never reaches the gather: the other rank's gather ends with an
+    error after the process-group timeout, while the staller is still asleep."""
+    out = _run("stalls")
+    state, t_stall = out[1]
+    msg, t_err = out[0]
+    assert state == "stalled" and msg.startswith("error"), (state, msg)
+    assert t_err - t_stall < 12.0  # before the staller wakes up: a timeout, not a hang
