@@ -157,6 +157,7 @@ _SIGNATURES = {
     "bitnet_attention_prefill_varlen": (
         _c_int, [_c_void_p, _c_void_p, _c_void_p, _c_int, _c_void_p, _c_int, _c_int, _c_int, _c_int, _c_int, _c_float,
                  _c_void_p, _c_void_p]),
+    "bitnet_selftest_bounded_wait": (_c_int, [ctypes.c_longlong, _c_void_p]),
     "bitnet_lm_head_bytes": (_c_size_t, [_c_int, _c_int]),
     "bitnet_pack_lm_head": (_c_int, [_c_void_p, _c_int, _c_int, _c_void_p, _c_void_p]),
     "bitnet_embed_gather": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_int, _c_int, _c_void_p, _c_void_p]),

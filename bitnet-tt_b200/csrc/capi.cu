@@ -136,6 +136,23 @@ inline int round_up(int x, int m) { return (x + m - 1) / m * m; }
 int act_rows_of(int M) { return M <= 256 ? round_up(M, 16) : round_up(M, 256); }
 int act_tile_of(int M) { return M <= 256 ? round_up(M, 16) : 256; }
 
+// One CTA waits on an mbarrier that nothing arrives on; the bounded wait gives
+// up after limit_cycles and records the timeout (site 900), then returns.
+__global__ void selftest_wait_kernel(long long limit_cycles) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const long long t0 = clock64();
+    bool done = mbar_try_wait(&bar, 0);
+    while (!done && clock64() - t0 <= limit_cycles) done = mbar_try_wait(&bar, 0);
+    if (!done) record_error(DEV_ERR_TIMEOUT, 900);
+  }
+}
+
 int to_dev_segments(const bitnet_segments_t* s, int N, int epilogue, bitnet_segments_dev* out) {
   memset(out, 0, sizeof(*out));
   if (s == nullptr) {
@@ -298,6 +315,13 @@ int bitnet_last_device_status(int* site) {
   if (st == DEV_ERR_TIMEOUT) return BITNET_ERR_DEVICE_TIMEOUT;
   if (st == DEV_ERR_BOUNDS) return BITNET_ERR_INVALID_ARGUMENT;
   return BITNET_OK;
+}
+
+int bitnet_selftest_bounded_wait(long long limit_cycles, bitnet_stream_t stream) {
+  DevInfo* d;
+  if (int e = device_info(&d)) return e;
+  if (limit_cycles < 1 || limit_cycles > (1LL << 31)) return BITNET_ERR_INVALID_ARGUMENT;
+  return launch(selftest_wait_kernel, dim3(1), dim3(32), 0, stream, 1, limit_cycles);
 }
 
 int bitnet_set_pdl(int enable) {

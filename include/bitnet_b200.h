@@ -66,6 +66,13 @@ int bitnet_last_device_status(int* site);
 /* Text of the last CUDA runtime failure reported as BITNET_ERR_CUDA on the
  * calling thread (the failing call, cudaGetErrorString, code). */
 const char* bitnet_last_cuda_error(void);
+/* Self-test of the bounded waits (no reference counterpart): launches one CTA
+ * whose mbarrier wait can never complete (nothing arrives on it).  The wait
+ * gives up after limit_cycles SM clocks (1 .. 2^31), records
+ * BITNET_ERR_DEVICE_TIMEOUT with site 900 in the device status word, and the
+ * kernel returns -- how every wait of the library's kernels ends when it runs
+ * out, shown without faulting or hanging the GPU.  The context stays usable. */
+int bitnet_selftest_bounded_wait(long long limit_cycles, bitnet_stream_t stream);
 
 /* ---- process-wide launch options (no reference counterpart: ttnn chooses
  * program configs internally) -------------------------------------------- */

@@ -247,3 +247,20 @@ def test_fused_bitlinear_small_m_equals_two_launches(cuda, m, epilogue, k):
         assert L.last_device_status()[0] == 0
         assert torch.equal(acc, acc_ref)
         assert torch.equal(y, y_ref)
+
+
+def test_bounded_wait_gives_up_with_a_status_and_the_context_stays_usable(cuda):
+    """A kernel whose wait can never complete (nothing arrives on its barrier)
+    ends the wait after its cycle limit, records BITNET_ERR_DEVICE_TIMEOUT (site
+    900) and returns; the status is read and cleared on the host, and the next
+    kernels run normally."""
+    L = _lib()
+    assert L.last_device_status() == (0, 0)
+    L.check(L.load().bitnet_selftest_bounded_wait(2_000_000, L.stream_handle()), "bitnet_selftest_bounded_wait")
+    assert L.last_device_status() == (-5, 900)
+    assert L.last_device_status() == (0, 0)  # read and cleared
+    x = rand_bf16((8, 256), seed=9)
+    q, s, rsum, _ = run_act_quant(x, None, 1e-5, cuda)
+    ref = ob.bitlinear(f32(x), None, 1e-5, np.zeros((1, 256), np.int8))
+    np.testing.assert_array_equal(q, ref["q"])
+    assert L.last_device_status() == (0, 0)
