@@ -411,14 +411,15 @@ class Batch32Generator:
 
     # ---- generation ----------------------------------------------------------
     def generate(self, input_ids, max_new_tokens: int = 128) -> np.ndarray:
-        """Greedy decode: returns [batch, max_new_tokens] token ids (equal-length prompts)."""
+        """Greedy decode: returns [batch, max_new_tokens] token ids.  Prompts may
+        differ in length (ragged prompts are prefilled packed, and every sequence
+        continues from its own position)."""
         prompts = self._prompts(input_ids)
-        if len({p.size for p in prompts}) != 1:
-            raise ValueError("generate() takes equal-length prompts; use prefill() + decode() for ragged ones")
-        if prompts[0].size + max_new_tokens > self.max_seq_len:
+        lmax = max(p.size for p in prompts)
+        if lmax + max_new_tokens > self.max_seq_len:
             raise ValueError("prompt + max_new_tokens exceeds the KV cache")
-        stats = GenerationStats(prompt_tokens=int(prompts[0].size) * self.batch_size)
-        self.set_context_limit(prompts[0].size + max_new_tokens)
+        stats = GenerationStats(prompt_tokens=int(sum(p.size for p in prompts)))
+        self.set_context_limit(lmax + max_new_tokens)
         torch.cuda.synchronize(self.device)
         t0 = time.perf_counter()
         self.prefill(prompts)

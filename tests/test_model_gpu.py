@@ -229,6 +229,9 @@ def test_ragged_prompts_prefill_matches_oracle(cuda, chunk):
         logits.append(gen.state.logits.float().cpu().clone())
     assert gen.state.positions.cpu().tolist() == [n + 3 for n in lens]
     dev_ids = np.stack(ids, 1)
+    gen2 = Batch32Generator(model, batch_size=len(lens), max_seq_len=96)
+    gen2.prefill_chunk_tokens = chunk
+    np.testing.assert_array_equal(gen2.generate(prompts, 4), dev_ids)  # the same through generate()
 
     oracle = om.OracleBitNet(cfg, sd, max_len=96)
     caches = oracle.new_cache(len(lens))
