@@ -246,7 +246,7 @@ int dispatch_tc(TcParams p, int ntile_n, int ntile_m, bitnet_stream_t st, const 
     // About 1.25 CTAs per SM: a K split cuts each CTA's chain of MMA stages,
     // and two CTAs share an SM (256 tensor-memory columns each) when there are
     // more CTAs than SMs.  Measured on B200 at 32 tokens: qkv 30 tiles -> 6,
-    // o_proj / down 20 tiles -> 8, gate_up 108 tiles -> 2.
+    // o_proj / down 20 tiles -> 8 (4, 6 and 8 tried at the whole-step level).
     split = 1;
     if (ntile_m == 1 && p.T <= 64) {
       split = (5 * dev.sms / 4 + tiles / 2) / tiles;
@@ -254,6 +254,12 @@ int dispatch_tc(TcParams p, int ntile_n, int ntile_m, bitnet_stream_t st, const 
       if (split > by_k) split = by_k;
       if (split > 8) split = 8;
       if (split < 1) split = 1;
+      // With >= 0.7 CTAs per SM already, no split: each CTA's whole K range then
+      // sits in its ring, fetched before griddepcontrol.wait, and the partial-sum
+      // exchange disappears.  Measured at 32 tokens: gate_up (108 tiles) alone
+      // 10.0 -> 11.1 us, but the decode step 17,290 -> 17,440 tok/s, because the
+      // weight fetch overlaps the preceding act-quant launch.
+      if (tiles * 10 >= dev.sms * 7) split = 1;
     }
   }
   // K chunks per stage.  Halving the stage for 256-token tiles (twice the
