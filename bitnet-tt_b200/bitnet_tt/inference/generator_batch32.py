@@ -159,8 +159,8 @@ class Batch32Generator:
 
     def set_context_limit(self, n: int) -> None:
         """Bound the positions the next steps reach (positions + 1 <= n).  The
-        attention splits the context in blocks of 256 keys, so the limit is
-        rounded up to that; a new limit re-captures the decode graph."""
+        attention sizes its grid by the limit in blocks of 256 keys, so the
+        limit is rounded up to that; a new limit re-captures the decode graph."""
         n = min(self.max_seq_len, max(1, -(-int(n) // 256) * 256))
         if n != self.context_limit:
             self.context_limit = n

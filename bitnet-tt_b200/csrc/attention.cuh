@@ -2,9 +2,13 @@
 //
 // Work unit (b, g, s): the G = n_heads / n_kv_heads query heads that share KV
 // head g (HF repeat_kv grouping: query head h uses KV head h / G) of sequence b,
-// over keys [s * ATT_SPLIT_KEYS, (s + 1) * ATT_SPLIT_KEYS).  Only the
-// ceil(L / ATT_SPLIT_KEYS) units whose range holds keys do work
-// (L = positions[b] + 1).  A unit runs on 4 warps:
+// over part s of its L = positions[b] + 1 keys.  The grid has `nsplit` units
+// per (b, g), chosen on the host from B * n_kv_heads and max_ctx
+// (att_grid_splits); a sequence is cut into min(nsplit, ceil(L / 256)) parts
+// of equal length in whole 16-key tiles (att_parts), and units past its last
+// part return at once.  So a long context over many sequences runs as one
+// long unit per (b, g), and a few sequences spread over the GPU.  A unit runs
+// on 4 warps:
 //   1. RoPE (HF half-split convention, bf16 op-by-op like transformers'
 //      apply_rotary_pos_emb on bf16 tensors):
 //        out[i]    = bf16(bf16(x[i] * cos_i)    + bf16(-x[i+64] * sin_i))
@@ -28,6 +32,8 @@
 //      of (b, g) to finish (a counter in the workspace, reset by that unit)
 //      merges the parts.
 #pragma once
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace bitnet {
@@ -37,10 +43,17 @@ constexpr int ATT_WARPS = ATT_THREADS / 32;
 constexpr int ATT_D = 128;
 constexpr int ATT_MAX_G = 8;
 constexpr int ATT_TILE = 16;                         // keys per tile
-constexpr int ATT_TILES_PER_WARP = 4;
 constexpr int ATT_NBUF = 2;                          // tiles in flight per warp
 constexpr int ATT_TILE_BYTES = ATT_TILE * ATT_D * 2; // K (or V) of one tile
-constexpr int ATT_SPLIT_KEYS = ATT_WARPS * ATT_TILE * ATT_TILES_PER_WARP;  // keys per unit
+constexpr int ATT_MIN_SPLIT = 256;                   // keys: a part is at least 4 tiles per warp
+// The split-count model (att_grid_splits).  Three 66 KB units fit on an SM,
+// so a B200 (148 SMs) holds 444 at once; a unit costs its keys plus about
+// 128 keys' worth of fixed work (RoPE, pipeline fill, the partial-state round
+// trip and the merge).  Fewer, longer units pay that less often: at 256
+// sequences x 4K keys one unit per (b, g) beats 16 units of 256 keys by a
+// fifth of the decode step, and 7 units of 620 keys by a sixth.
+constexpr int ATT_SLOTS = 444;
+constexpr int ATT_UNIT_COST = 128;
 constexpr int ATT_TILES_BYTES = ATT_WARPS * ATT_NBUF * 2 * ATT_TILE_BYTES;  // 64 KB
 constexpr int ATT_QROW = 136;                        // bf16 per query row in shared memory (padded)
 
@@ -61,6 +74,39 @@ struct AttnParams {
 };
 
 __host__ __device__ __forceinline__ int att_part_floats(int G) { return 2 * G + G * ATT_D; }
+
+// Units per (b, g) in the grid: the s in 1 .. ceil(max_ctx / 256) with the
+// least modelled time, waves x unit length =
+// ceil(B n_kv s / ATT_SLOTS) x (ceil(max_ctx / s) + ATT_UNIT_COST), the
+// smallest s on a tie.  A wave that is barely begun costs a whole unit, so the
+// model avoids unit counts just past a multiple of the slots.
+inline int att_grid_splits(int B, int n_kv, int max_ctx) {
+  const long long pairs = (long long)B * n_kv;
+  const int smax = (int)std::max<long long>(1, ((long long)max_ctx + ATT_MIN_SPLIT - 1) / ATT_MIN_SPLIT);
+  int best_s = 1;
+  long long best = -1;
+  for (int s = 1; s <= smax; ++s) {
+    const long long waves = (pairs * s + ATT_SLOTS - 1) / ATT_SLOTS;
+    const long long cost = waves * (((long long)max_ctx + s - 1) / s + ATT_UNIT_COST);
+    if (best < 0 || cost < best) {
+      best = cost;
+      best_s = s;
+    }
+  }
+  return best_s;
+}
+
+// The parts of a sequence of L >= 1 keys: n = min(nsplit, ceil(L / 256)) cut
+// to `span` keys each (ceil(L / n) rounded up to a whole tile); the last part
+// is the shorter one, and nparts = ceil(L / span) <= n, so every part is
+// non-empty and part nparts - 1 holds key L - 1.
+__host__ __device__ __forceinline__ void att_parts(int L, int nsplit, int& nparts, int& span) {
+  int n = (L + ATT_MIN_SPLIT - 1) / ATT_MIN_SPLIT;
+  if (n > nsplit) n = nsplit;
+  if (n < 1) n = 1;
+  span = ((L + n - 1) / n + ATT_TILE - 1) / ATT_TILE * ATT_TILE;
+  nparts = (L + span - 1) / span;
+}
 
 // Shared memory of one unit besides its tiles: rotated queries bf16
 // [G][ATT_QROW] | new key, new value (bf16) | mbarriers [warp][buffer].
@@ -137,7 +183,7 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 }
 
 // One unit on threads t = 0..127 of the caller, synchronised by barrier `bar`.
-// Warp w takes the tiles w, w + 4, w + 8, w + 12 of the unit's range, two in
+// Warp w takes the tiles w, w + 4, w + 8, ... of the unit's range, two in
 // flight, with an online softmax over them.  Both products run on the tensor
 // cores (mma.sync m16n8k16, bf16 in, fp32 accumulate):
 //   S^T [heads x keys] = Q K^T   (A = queries, rows 0..G-1 of 16; B = K rows)
@@ -160,9 +206,10 @@ __device__ __forceinline__ bool attn_unit(const AttnParams& p, int b, int g, int
     return true;
   }
   const int L = pos + 1;
-  const int nparts = (L + ATT_SPLIT_KEYS - 1) / ATT_SPLIT_KEYS;
+  int nparts = 1, span = L;  // one unit per (b, g): no divides before the first copies
+  if (p.nsplit > 1) att_parts(L, p.nsplit, nparts, span);
   if (sp >= nparts) return true;
-  const int r0 = sp * ATT_SPLIT_KEYS, r1 = min(L, r0 + ATT_SPLIT_KEYS);
+  const int r0 = sp * span, r1 = min(L, r0 + span);
   const int ntiles = (r1 - r0 + ATT_TILE - 1) / ATT_TILE;
   const int ntw = ntiles > warp ? (ntiles - warp + ATT_WARPS - 1) / ATT_WARPS : 0;  // tiles of this warp
 

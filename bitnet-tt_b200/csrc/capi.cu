@@ -507,11 +507,9 @@ int bitnet_bitlinear(const void* x, int M, int K, const void* gamma, float eps, 
                             path, stream);
 }
 
-static int att_nsplit(int max_ctx) { return (max_ctx + ATT_SPLIT_KEYS - 1) / ATT_SPLIT_KEYS; }
-
 size_t bitnet_gqa_decode_workspace_bytes(int B, int n_heads, int n_kv_heads, int max_ctx) {
   if (B <= 0 || n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads != 0 || max_ctx <= 0) return 0;
-  const int S = att_nsplit(max_ctx);
+  const int S = att_grid_splits(B, n_kv_heads, max_ctx);
   if (S <= 1) return 0;
   const size_t counters = ((size_t)B * n_kv_heads * sizeof(int) + 255) / 256 * 256;
   return counters + (size_t)B * n_kv_heads * S * att_part_floats(n_heads / n_kv_heads) * sizeof(float);
@@ -547,7 +545,7 @@ int bitnet_gqa_decode_attention(const void* qkv, int B, int n_heads, int n_kv_he
   p.v_cache = (uint16_t*)v_cache;
   p.max_len = max_len;
   p.max_ctx = max_ctx;
-  p.nsplit = att_nsplit(max_ctx);
+  p.nsplit = att_grid_splits(B, n_kv_heads, max_ctx);
   p.scale = scale;
   const size_t counters = ((size_t)B * n_kv_heads * sizeof(int) + 255) / 256 * 256;
   p.ws_count = ws_need > 0 ? (int*)workspace : nullptr;
@@ -1039,7 +1037,7 @@ extern "C" int bitnet_decode_plan_create(const bitnet_decode_desc_t* d, bitnet_d
   a.rope_len = d->rope_len;
   a.max_len = d->max_len;
   a.max_ctx = max_ctx;
-  a.nsplit = (max_ctx + ATT_SPLIT_KEYS - 1) / ATT_SPLIT_KEYS;
+  a.nsplit = att_grid_splits(B, NKV, max_ctx);
   a.scale = 1.0f / sqrtf((float)ATT_D);
   const size_t counters = ((size_t)B * NKV * sizeof(int) + 255) / 256 * 256;
   a.ws_count = att_ws > 0 ? (int*)d->attn_workspace : nullptr;

@@ -165,8 +165,10 @@ int bitnet_bitlinear_noalloc(const void* x, int M, int K, const void* gamma, flo
  * Replaces nlp_create_qkv_heads_decode + rotary_embedding_llama +
  * paged_update_cache + scaled_dot_product_attention_decode +
  * nlp_concat_heads_decode (src/bitnet_tt/layers/attention.py:1040-1262; the
- * SDPA decode's chunked grid, attention.py:670-708, becomes a split of the
- * context over CTAs of 256 keys with an in-kernel merge).
+ * SDPA decode's chunked grid, attention.py:670-708, becomes a split of each
+ * context over up to ceil(max_ctx / 256) CTAs with an in-kernel merge; the
+ * count per (sequence, KV head) minimises waves x unit length over the GPU,
+ * so many long contexts run one CTA each and a few spread wide).
  * qkv: bf16 [B, (n_heads + 2*n_kv_heads) * head_dim] (Q | K | V, already scaled),
  * 4-byte aligned.
  * positions: int32 [B], the position of the token being decoded per sequence.
@@ -178,7 +180,8 @@ int bitnet_bitlinear_noalloc(const void* x, int M, int K, const void* gamma, flo
  * grid small.  A position at or above it is a device bounds error.
  * workspace: bitnet_gqa_decode_workspace_bytes(B, n_heads, n_kv_heads, max_ctx)
  * bytes, 16-byte aligned, ZEROED before its first use (the kernel leaves it
- * zeroed); may be NULL when that size is 0 (max_ctx <= 256).
+ * zeroed); may be NULL when that size is 0 (one CTA per (sequence, KV head):
+ * max_ctx <= 256, or enough sequences to fill the GPU).
  * out: bf16 [B, n_heads * head_dim].  head_dim must be 128. */
 size_t bitnet_gqa_decode_workspace_bytes(int B, int n_heads, int n_kv_heads, int max_ctx);
 int bitnet_gqa_decode_attention(const void* qkv, int B, int n_heads, int n_kv_heads, int head_dim,

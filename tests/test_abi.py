@@ -45,11 +45,14 @@ def test_status_strings_and_sizes():
     # per-CTA (max, idx) pairs for up to 160 CTAs, then the hidden states tiled (K x T bf16)
     assert _lib.argmax_workspace_bytes(32, 2560, 128256) == 160 * 32 * 8 + 2560 * 32 * 2
     assert lib.bitnet_packed_weight_bytes(0, 5) == 0
-    # attention: no workspace up to 256 keys; else 256-byte aligned counters,
-    # then per (sequence, KV head, split of 256 keys) 2G + 128G floats
+    # attention: units per (sequence, KV head) from the wave model (at most one
+    # per 256 keys); with more than one, 256-byte aligned counters, then per
+    # unit 2G + 128G floats
     assert _lib.gqa_decode_workspace_bytes(32, 20, 5, 256) == 0
     assert _lib.gqa_decode_workspace_bytes(32, 20, 5, 257) == 768 + 32 * 5 * 2 * (8 + 512) * 4
-    assert _lib.gqa_decode_workspace_bytes(32, 20, 5, 4096) == 768 + 32 * 5 * 16 * (8 + 512) * 4
+    assert _lib.gqa_decode_workspace_bytes(32, 20, 5, 4096) == 768 + 32 * 5 * 5 * (8 + 512) * 4
+    assert _lib.gqa_decode_workspace_bytes(1, 20, 5, 4096) == 256 + 5 * 16 * (8 + 512) * 4
+    assert _lib.gqa_decode_workspace_bytes(256, 20, 5, 4352) == 0  # 1280 units of 4352 keys: one split
     assert _lib.gqa_decode_workspace_bytes(32, 20, 3, 4096) == 0  # heads not a multiple of KV heads
 
 

@@ -96,6 +96,21 @@ def test_attention_split_context_ragged(cuda):
     _attention_case(cuda, 6, 20, 5, 4096, [0, 255, 256, 1000, 2047, 4095], seed=3)
 
 
+@pytest.mark.parametrize("b,max_len,units", [(32, 3000, 5), (150, 1024, 1)])
+def test_attention_split_policy_long_units(cuda, b, max_len, units):
+    # 32 x 3000 keys: five units of up to 608 keys per (sequence, KV head);
+    # 150 x 1024: 750 (sequence, KV head) pairs fill the GPU, so one unit of up
+    # to 1024 keys (16 tiles per warp) each
+    from bitnet_tt import _lib
+
+    want = 0 if units == 1 else 768 + b * 5 * units * (8 + 512) * 4
+    assert _lib.gqa_decode_workspace_bytes(b, 20, 5, max_len) == want
+    rng = np.random.default_rng(b)
+    pos = sorted(rng.integers(0, max_len, size=b).tolist())
+    pos[0], pos[1], pos[-1] = 0, 256, max_len - 1
+    _attention_case(cuda, b, 20, 5, max_len, pos, seed=b)
+
+
 def test_attention_split_repeated_calls(cuda):
     # the workspace counters must return to zero so that later calls merge correctly
     for rep in range(3):
@@ -113,6 +128,7 @@ def test_attention_position_beyond_max_ctx_is_a_device_error(cuda):
     cos, sin = half_split_tables(d, max_len, 500000.0)
     out = torch.empty((b, nh * d), dtype=torch.bfloat16, device=cuda)
     pos = torch.tensor([3, 300], dtype=torch.int32, device=cuda)
+    # max_ctx 128: a single unit per (sequence, KV head), so no workspace
     _lib.gqa_decode_attention(qkv, nh, nkv, d, pos, cos.to(cuda), sin.to(cuda), kd, vd, 1.0, out, 128, None)
     torch.cuda.synchronize()
     code, site = _lib.last_device_status()
