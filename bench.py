@@ -47,9 +47,14 @@ FALLBACK_HBM_GBS = 6650.0
 FALLBACK_BF16_TFLOPS = 1590.0
 
 # DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) from one ncu
-# capture of each kernel class inside the decode step (caches flushed before the
-# captured launch); profiles/decode_step_dram_bytes_b32.md has the capture.
-# None where no capture of the current kernel exists.
+# capture of each kernel class inside the batch-32 decode step (caches flushed before
+# the captured launch); profiles/decode_step_dram_bytes_b32.md has the capture.  Used
+# only at that batch; None where no capture of the current kernel exists.
+NCU_TRAFFIC_BATCH = 32
+# Decode attention: DRAM bytes / algorithmic bytes of one launch at config-4 contexts
+# (359,606,784 / 353,400,320; profiles/gqa_decode_attention_config4_64seq.md).  Every
+# K/V row is read once, so the traffic of a launch scales with the keys it reads.
+NCU_TRAFFIC_RATIO: dict[str, float] = {"attention": 359606784.0 / 353400320.0}
 NCU_TRAFFIC_BYTES: dict[str, float | None] = {
     "bitlinear_qkv": 2610688.0,
     "bitlinear_o": 1955840.0,
@@ -339,9 +344,11 @@ def kernel_rooflines(gen, args, hbm_peak: float) -> dict:
         ms = time_graph(g, 20)
         per = ms / launches_per_replay
         gbs = bytes_per_launch / (per * 1e-3) / 1e9
+        traffic = NCU_TRAFFIC_BYTES.get(name) if b == NCU_TRAFFIC_BATCH else None
+        if name in NCU_TRAFFIC_RATIO:
+            traffic = bytes_per_launch * NCU_TRAFFIC_RATIO[name]
         res[name] = {"us_per_launch": per * 1e3, "bytes_per_launch": bytes_per_launch, "achieved_gbs": gbs,
-                     "frac": gbs / hbm_peak, "ms_per_step": per * count_per_step,
-                     "traffic": NCU_TRAFFIC_BYTES.get(name)}
+                     "frac": gbs / hbm_peak, "ms_per_step": per * count_per_step, "traffic": traffic}
         del g
 
     nl = len(m.layers)
