@@ -57,11 +57,11 @@ NCU_TRAFFIC_BATCH = 32
 NCU_TRAFFIC_RATIO: dict[str, float] = {"attention": 359606784.0 / 353400320.0}
 NCU_TRAFFIC_BYTES: dict[str, float | None] = {
     "bitlinear_qkv": 2610688.0,
-    "bitlinear_o": 1955840.0,
-    "bitlinear_gate_up": 9004800.0,
-    "bitlinear_down": 4880384.0,
-    "act_quant": 192512.0,
-    "lm_head": 659942144.0,
+    "bitlinear_o": 1956096.0,
+    "bitlinear_gate_up": 9000192.0,
+    "bitlinear_down": 4880896.0,
+    "act_quant": 193792.0,
+    "lm_head": 659862528.0,
 }
 
 # Kernel classes timed by kernel_rooflines, grouped by the kernel (template
