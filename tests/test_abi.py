@@ -53,6 +53,9 @@ def test_status_strings_and_sizes():
     assert _lib.gqa_decode_workspace_bytes(32, 20, 5, 4096) == 768 + 32 * 5 * 5 * (8 + 512) * 4
     assert _lib.gqa_decode_workspace_bytes(1, 20, 5, 4096) == 256 + 5 * 16 * (8 + 512) * 4
     assert _lib.gqa_decode_workspace_bytes(256, 20, 5, 4352) == 0  # 1280 units of 4352 keys: one split
+    # the counts measured best at config-4 contexts per GPU: 32 and 64 sequences -> 5 and 4 units
+    assert _lib.gqa_decode_workspace_bytes(32, 20, 5, 4352) == 768 + 32 * 5 * 5 * (8 + 512) * 4
+    assert _lib.gqa_decode_workspace_bytes(64, 20, 5, 4352) == 1280 + 64 * 5 * 4 * (8 + 512) * 4
     assert _lib.gqa_decode_workspace_bytes(32, 20, 3, 4096) == 0  # heads not a multiple of KV heads
 
 
