@@ -113,6 +113,8 @@ _SIGNATURES = {
     "bitnet_act_rows": (_c_int, [_c_int]),
     "bitnet_pack_ternary": (_c_int, [_c_void_p, _c_int, _c_int, _c_void_p, _c_void_p]),
     "bitnet_pack_from_canonical": (_c_int, [_c_void_p, _c_int, _c_int, _c_void_p, _c_void_p]),
+    "bitnet_tilized_weight_bytes": (_c_size_t, [_c_int, _c_int]),
+    "bitnet_pack_from_tilized": (_c_int, [_c_void_p, _c_int, _c_int, _c_void_p, _c_void_p]),
     "bitnet_act_quant": (
         _c_int,
         [_c_void_p, _c_int, _c_int, _c_int, _c_void_p, _c_float, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
@@ -272,6 +274,21 @@ def pack_from_canonical(canonical: torch.Tensor, n: int, k: int) -> torch.Tensor
     out = torch.empty(packed_weight_bytes(n, k), dtype=torch.uint8, device=canonical.device)
     check(load().bitnet_pack_from_canonical(ptr(canonical.contiguous()), n, k, ptr(out), stream_handle()),
           "bitnet_pack_from_canonical")
+    return out
+
+
+def tilized_weight_bytes(n: int, k: int) -> int:
+    return int(load().bitnet_tilized_weight_bytes(n, k))
+
+
+def pack_from_tilized(tiles: torch.Tensor, n: int, k: int) -> torch.Tensor:
+    """The reference's Tensix tile format (uint8 [tiles, 256], kernels/pack.py
+    pack_ternary_tilized of W [n, k]) -> device weight layout."""
+    if tiles.dtype != torch.uint8 or tiles.numel() != tilized_weight_bytes(n, k):
+        raise ValueError("pack_from_tilized expects uint8 tiles of tilized_weight_bytes(n, k) bytes")
+    out = torch.empty(packed_weight_bytes(n, k), dtype=torch.uint8, device=tiles.device)
+    check(load().bitnet_pack_from_tilized(ptr(tiles.contiguous()), n, k, ptr(out), stream_handle()),
+          "bitnet_pack_from_tilized")
     return out
 
 

@@ -109,6 +109,17 @@ class Linear:
         wt = weight_t if isinstance(weight_t, torch.Tensor) else torch.from_numpy(np.asarray(weight_t))
         self.load_ternary(torch.round(wt.float()).clamp(-1, 1).to(torch.int8).t().contiguous(), scale)
 
+    def load_tilized(self, tiles, scale: float = 1.0) -> None:
+        """Load a ternary weight already in the reference's Tensix tile format
+        (uint8 [tiles, 256] from kernels/pack.py pack_ternary_tilized of W [out, in],
+        the tiling the packed_ternary load_weights stores, bitlinear.py:211-251),
+        re-laid out on the device without unpacking on the host."""
+        t = _as_device(tiles, self.device, torch.uint8).reshape(-1)
+        self.weight = _lib.pack_from_tilized(t, self.out_features, self.in_features)
+        self.weight_scale = float(scale)
+        self._segments = None
+        self._use_packed_ternary = True
+
     def set_segments(self, segments: list[tuple[int, float]] | None) -> None:
         """Per-row-range scales of a fused projection: [(end_row, scale), ...]."""
         self._segments = segments

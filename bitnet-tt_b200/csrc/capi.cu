@@ -32,7 +32,7 @@ using namespace bitnet;
 
 namespace {
 
-constexpr int kAbiVersion = 2;
+constexpr int kAbiVersion = 3;
 constexpr int kMaxDevices = 64;
 constexpr size_t kMaxDynSmem = 232448;  // 227 KB, the sm_100 per-CTA opt-in limit
 
@@ -383,6 +383,24 @@ int bitnet_pack_from_canonical(const uint8_t* canonical, int N, int K, uint8_t* 
   const size_t words = (size_t)Npad * KC * 4;
   pack_from_canonical_kernel<<<grid_for(words, 256), 256, 0, (cudaStream_t)stream>>>(
       canonical, N, K, Npad, KC, reinterpret_cast<uint32_t*>(w_packed));
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? BITNET_OK : cuda_fail(e, "kernel launch");
+}
+
+size_t bitnet_tilized_weight_bytes(int N, int K) {
+  if (N <= 0 || K <= 0) return 0;
+  return (size_t)((K + 31) / 32) * (size_t)((N + 31) / 32) * 256u;
+}
+
+int bitnet_pack_from_tilized(const uint8_t* tiles, int N, int K, uint8_t* w_packed, bitnet_stream_t stream) {
+  DevInfo* d;
+  if (int e = device_info(&d)) return e;
+  if (!tiles || !w_packed || N <= 0 || K <= 0) return BITNET_ERR_INVALID_ARGUMENT;
+  if (!aligned(w_packed, 16)) return BITNET_ERR_ALIGNMENT;
+  const int Npad = round_up(N, 128), KC = round_up(K, 64) / 64;
+  const size_t words = (size_t)Npad * KC * 4;
+  pack_from_tilized_kernel<<<grid_for(words, 256), 256, 0, (cudaStream_t)stream>>>(
+      tiles, N, K, Npad, KC, reinterpret_cast<uint32_t*>(w_packed));
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? BITNET_OK : cuda_fail(e, "kernel launch");
 }

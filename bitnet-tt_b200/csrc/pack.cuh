@@ -75,6 +75,47 @@ __global__ void pack_from_canonical_kernel(const uint8_t* __restrict__ canon, in
   }
 }
 
+// Same output, reading the reference's Tensix tile format (kernels/pack.py:101-155,
+// consumed by kernels/device/reader_ternary_in1.cpp:44-55, 86-113): the transposed
+// matrix W^T [K, N] cut into 32 x 32 tiles, tile (kt, nt) at index kt * Nt + nt
+// (Nt = ceil(N / 32)), 256 bytes per tile.  Inside a tile the four 16 x 16 faces
+// (top-left, top-right, bottom-left, bottom-right) follow one another, each row
+// major; element e of that order sits in byte e / 4 at bits 6 - 2 * (e % 4)
+// (MSB first), with the Tensix codes 0b00 = 0, 0b01 = +1, 0b10 = -1 (0b11 is
+// reserved and read as 0, as the reference's lookup table does).
+__device__ __forceinline__ uint32_t tilized_code(const uint8_t* __restrict__ tiles, int n, int k, int Nt) {
+  const int kt = k >> 5, nt = n >> 5, r = k & 31, c = n & 31;
+  const int e = ((r >> 4) * 2 + (c >> 4)) * 256 + (r & 15) * 16 + (c & 15);
+  const uint32_t t = (tiles[((size_t)kt * Nt + nt) * 256u + (e >> 2)] >> (6 - 2 * (e & 3))) & 3u;
+  return t == 1u ? 2u : (t == 2u ? 0u : 1u);  // Tensix code -> device code w + 1
+}
+
+__global__ void pack_from_tilized_kernel(const uint8_t* __restrict__ tiles, int N, int K, int Npad, int KC,
+                                         uint32_t* __restrict__ out) {
+  const int Nt = (N + 31) >> 5;
+  const size_t total = (size_t)Npad * KC * 4;
+  for (size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+       idx += (size_t)gridDim.x * blockDim.x) {
+    const int wi = (int)(idx & 3);
+    const size_t cell = idx >> 2;
+    const int r = (int)(cell & 127);
+    const size_t blk = cell >> 7;
+    const int kc = (int)(blk % KC);
+    const int nb = (int)(blk / KC);
+    const int n = nb * 128 + r;
+    const int kbase = kc * 64 + wi * 16;
+    uint32_t word = 0;
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      const int k = kbase + e;
+      const uint32_t code = (n < N && k < K) ? tilized_code(tiles, n, k, Nt) : 1u;
+      const int j = e >> 2, b = e & 3;
+      word |= code << (8 * b + 2 * j);
+    }
+    out[idx] = word;
+  }
+}
+
 // lm_head / embedding table: bf16 [V, K] -> [V/128 tiles][K/8 chunks][128 rows][8 bf16].
 // Each (tile, chunk) block is 2 KB of 16 tcgen05 core matrices (8 rows x 16 B).
 __global__ void pack_lm_head_kernel(const uint16_t* __restrict__ w, int V, int K, int Vpad, int KC8,

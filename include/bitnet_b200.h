@@ -104,6 +104,16 @@ int bitnet_pack_ternary(const int8_t* w_q, int N, int K, uint8_t* w_packed, bitn
  * row-major [N, K] matrix flattened, 4 codes (w + 1) per byte, MSB first. */
 int bitnet_pack_from_canonical(const uint8_t* canonical, int N, int K, uint8_t* w_packed,
                                bitnet_stream_t stream);
+/* Same, from the reference's Tensix tile format (src/bitnet_tt/kernels/pack.py:101-155
+ * pack_ternary_tilized, read by src/bitnet_tt/kernels/device/reader_ternary_in1.cpp:44-55,
+ * 86-113; the tiled ternary weight the packed_ternary Linear.load_weights stores,
+ * src/bitnet_tt/layers/bitlinear.py:211-251): W^T [K, N] in 32 x 32 tiles, tile
+ * (kt, nt) at index kt * ceil(N/32) + nt, 256 bytes each; inside a tile the four
+ * 16 x 16 faces TL, TR, BL, BR, each row major, 4 codes per byte MSB first,
+ * codes 0b00 = 0, 0b01 = +1, 0b10 = -1 (0b11 reads as 0).  `tiles` holds
+ * bitnet_tilized_weight_bytes(N, K) bytes (K and N padded to 32 with zeros). */
+size_t bitnet_tilized_weight_bytes(int N, int K);
+int bitnet_pack_from_tilized(const uint8_t* tiles, int N, int K, uint8_t* w_packed, bitnet_stream_t stream);
 
 /* ---- fused RMSNorm + per-token int8 absmax quantisation --------------------
  * Replaces ttnn.rms_norm (src/bitnet_tt/layers/bitlinear.py:433-461) feeding

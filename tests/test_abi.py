@@ -28,11 +28,34 @@ def test_library_exports_every_declared_symbol():
     assert sorted(_lib.exported_symbols()) == names
 
 
+def header_arity() -> dict[str, int]:
+    """Number of parameters of every function the header declares."""
+    src = open(os.path.join(ROOT, "include", "bitnet_b200.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    out = {}
+    for name, params in re.findall(r"\b(bitnet_[a-z0-9_]+)\s*\(([^)]*)\)\s*;", src):
+        params = params.strip()
+        out[name] = 0 if params in ("", "void") else params.count(",") + 1
+    return out
+
+
+def test_binding_arity_matches_header():
+    """Each ctypes signature declares as many arguments as the C prototype."""
+    from bitnet_tt import _lib
+
+    arity = header_arity()
+    assert sorted(arity) == header_functions()
+    wrong = {n: (len(_lib._SIGNATURES[n][1]), k) for n, k in arity.items() if len(_lib._SIGNATURES[n][1]) != k}
+    assert not wrong, f"binding vs header argument counts differ: {wrong}"
+
+
 def test_status_strings_and_sizes():
     from bitnet_tt import _lib
 
     lib = _lib.load()
-    assert lib.bitnet_abi_version() == 2
+    assert lib.bitnet_abi_version() == 3
+    assert _lib.tilized_weight_bytes(2560, 2560) == 80 * 80 * 256
+    assert _lib.tilized_weight_bytes(50, 100) == 8 * 256  # K and N padded to 32
     assert _lib.status_string(0) == "ok"
     assert "invalid argument" in _lib.status_string(-1)
     assert "unknown" in _lib.status_string(-99)

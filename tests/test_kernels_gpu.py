@@ -53,6 +53,45 @@ def test_pack_from_canonical_bytes(cuda, n, k):
     np.testing.assert_array_equal(dev.cpu().numpy(), ob.device_pack(w))
 
 
+@pytest.mark.parametrize("name,n,k", [("tl", 64, 128), ("tlo", 50, 100)])
+def test_pack_from_tilized_golden_tiles(cuda, golden, name, n, k):
+    """The reference's own tilized bytes (golden vectors made by its kernels/pack.py)
+    re-laid out on the device equal the device packing of the same codes."""
+    L = _lib()
+    tiles = golden[f"{name}_packed"]
+    w = golden[f"{name}_in"].astype(np.int8)
+    assert tiles.size == L.tilized_weight_bytes(n, k)
+    dev = L.pack_from_tilized(torch.from_numpy(np.ascontiguousarray(tiles)).to(cuda), n, k)
+    np.testing.assert_array_equal(dev.cpu().numpy(), ob.device_pack(w))
+
+
+@pytest.mark.parametrize("n,k", [(640, 2560), (2560, 6912), (33, 95)])
+def test_pack_from_tilized_bytes(cuda, n, k):
+    L = _lib()
+    w = rand_ternary(n, k, seed=n + 3 * k)
+    tiles, _ = oq.pack_ternary_tilized(w, 1.0)
+    tiles[0, 0] |= 0b11  # a reserved code (last element of the first group) reads as a zero weight
+    w_ref = w.copy()
+    w_ref[3, 0] = 0  # tile element (k=0, n=3): face 0, index 3 -> bits 1..0 of byte 0
+    dev = L.pack_from_tilized(torch.from_numpy(tiles).to(cuda), n, k)
+    np.testing.assert_array_equal(dev.cpu().numpy(), ob.device_pack(w_ref))
+
+
+def test_linear_load_tilized_matches_load_weights(cuda):
+    from bitnet_tt.layers.bitlinear import Linear
+
+    rng = np.random.default_rng(12)
+    w = (0.02 * rng.standard_normal((384, 640))).astype(np.float32)
+    wq, s = oq.weight_quant_ternary(w)
+    tiles, _ = oq.pack_ternary_tilized(wq, float(s))
+    a, b = Linear(640, 384, cuda), Linear(640, 384, cuda)
+    a.load_weights(w)
+    b.load_tilized(tiles, float(s))
+    assert torch.equal(a.weight, b.weight) and a.weight_scale == b.weight_scale
+    x = rand_bf16((8, 640), seed=4)
+    assert torch.equal(a(x.to(cuda)), b(x.to(cuda)))
+
+
 # ---------------------------------------------------------------------------
 # fused RMSNorm + int8 absmax quantisation
 # ---------------------------------------------------------------------------
