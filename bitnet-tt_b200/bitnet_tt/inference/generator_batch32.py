@@ -397,15 +397,22 @@ class Batch32Generator:
             else:
                 self._prefill_ragged(prompts)
             return lens
-        t0 = 0
+        # Token by token through the decode step.  A sequence whose prompt is
+        # shorter than the longest one re-runs its last prompt token at its last
+        # prompt position on every remaining step: that step rewrites the same
+        # K/V row from the same inputs and produces the same first token, so when
+        # the loop ends every sequence holds its first generated token and sits
+        # at its own next position, as after the batched prefill.
         table = np.zeros((lmax, self.batch_size), dtype=np.int32)
         for b, p in enumerate(prompts):
             table[: p.size, b] = p
         table_d = torch.from_numpy(table).to(self.device)
-        lens_d = torch.from_numpy(lens.astype(np.int32)).to(self.device)
-        for t in range(t0, lmax):
-            # a sequence whose prompt is exhausted keeps its generated token
-            st.ids.copy_(torch.where(lens_d > t, table_d[t], st.ids))
+        last_d = torch.from_numpy((lens - 1).astype(np.int64)).to(self.device)
+        cols = torch.arange(self.batch_size, device=self.device)
+        for t in range(lmax):
+            idx = torch.clamp(last_d, max=t)  # per-sequence prompt index (and position) of this step
+            st.ids.copy_(table_d[idx, cols])
+            st.positions.copy_(idx.to(torch.int32))
             self.step()
         return lens
 

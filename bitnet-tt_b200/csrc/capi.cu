@@ -819,7 +819,10 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoallocBytes];
 // name is only a host-side stand-in, so the address is looked up once per
 // device with that device current and the looked-up pointer is what the
 // kernels receive.
-unsigned char* g_noalloc_ptr[kMaxDevices] = {};
+// Published with release / read with acquire, so a thread that sees a
+// non-null pointer also sees the completed look-up (double-checked locking
+// without a data race).
+std::atomic<unsigned char*> g_noalloc_ptr[kMaxDevices] = {};
 std::mutex g_noalloc_mu;
 
 int noalloc_scratch(unsigned char** out) {
@@ -827,16 +830,19 @@ int noalloc_scratch(unsigned char** out) {
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   if (dev < 0 || dev >= kMaxDevices) return BITNET_ERR_INVALID_ARGUMENT;
-  if (g_noalloc_ptr[dev] == nullptr) {
+  unsigned char* ptr = g_noalloc_ptr[dev].load(std::memory_order_acquire);
+  if (ptr == nullptr) {
     std::lock_guard<std::mutex> lk(g_noalloc_mu);
-    if (g_noalloc_ptr[dev] == nullptr) {
+    ptr = g_noalloc_ptr[dev].load(std::memory_order_relaxed);
+    if (ptr == nullptr) {
       void* p = nullptr;
       e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
       if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_noalloc_scratch)");
-      g_noalloc_ptr[dev] = static_cast<unsigned char*>(p);
+      ptr = static_cast<unsigned char*>(p);
+      g_noalloc_ptr[dev].store(ptr, std::memory_order_release);
     }
   }
-  *out = g_noalloc_ptr[dev];
+  *out = ptr;
   return BITNET_OK;
 }
 

@@ -221,11 +221,13 @@ def test_batched_prefill_matches_oracle(cuda, batch, plen):
             assert (d - ref[:, :, :plen]).norm() / ref[:, :, :plen].norm() < 2e-2
 
 
-@pytest.mark.parametrize("chunk", [20, 65536])
+@pytest.mark.parametrize("chunk", [20, 65536, 0])
 def test_ragged_prompts_prefill_matches_oracle(cuda, chunk):
     """Ragged prompts packed without padding (varlen RoPE / attention; chunk 20
     splits the batch into several prefill passes) against the oracle prefilling
-    each sequence on its own; then decode steps at the sequences' own positions."""
+    each sequence on its own; then decode steps at the sequences' own positions.
+    chunk 0: batched_prefill = False, every prompt token through the decode
+    step (short prompts re-run their last token while the longest finishes)."""
     from bitnet_tt.inference import Batch32Generator
 
     cfg = _small_cfg()
@@ -235,7 +237,8 @@ def test_ragged_prompts_prefill_matches_oracle(cuda, chunk):
     lens = [5, 12, 9, 1, 17, 6, 70, 8]
     prompts = [rng.integers(0, cfg.vocab_size, size=n) for n in lens]
     gen = Batch32Generator(model, batch_size=len(lens), max_seq_len=96, keep_logits=True)
-    gen.prefill_chunk_tokens = chunk
+    gen.prefill_chunk_tokens = chunk or 65536
+    gen.batched_prefill = chunk != 0
     gen.prefill(prompts)
     assert gen.state.positions.cpu().tolist() == lens
     ids, logits = [gen.state.ids.cpu().numpy().copy()], [gen.state.logits.float().cpu().clone()]
@@ -246,7 +249,8 @@ def test_ragged_prompts_prefill_matches_oracle(cuda, chunk):
     assert gen.state.positions.cpu().tolist() == [n + 3 for n in lens]
     dev_ids = np.stack(ids, 1)
     gen2 = Batch32Generator(model, batch_size=len(lens), max_seq_len=96)
-    gen2.prefill_chunk_tokens = chunk
+    gen2.prefill_chunk_tokens = chunk or 65536
+    gen2.batched_prefill = chunk != 0
     np.testing.assert_array_equal(gen2.generate(prompts, 4), dev_ids)  # the same through generate()
 
     oracle = om.OracleBitNet(cfg, sd, max_len=96)

@@ -53,7 +53,9 @@ def _call_both(cuda, m, k, n, epilogue, seed, path):
 @pytest.mark.parametrize("m,k,n,epi,path", [
     (32, 2560, 3840, 0, 2),   # decode QKV shape, tcgen05 path
     (32, 6912, 2560, 2, 2),   # decode down shape with the residual epilogue
-    (1, 2560, 13824, 1, 1),   # batch-1 gate/up with the ReLU^2 epilogue, SIMT path
+    (1, 2560, 13824, 1, 1),   # batch-1 gate/up, ReLU^2 epilogue: the fused SIMT launch (uses no scratch)
+    (3, 2500, 2560, 2, 1),    # SIMT path through the static scratch: K % 8 != 0 takes the act-quant
+                              # launch into the scratch, then the CUDA-core BitLinear reads it
 ])
 def test_noalloc_matches_allocating_entry_point_twice(cuda, m, k, n, epi, path):
     for call, seed in enumerate((11, 12)):  # two calls in a row, different inputs
