@@ -12,6 +12,13 @@ fp32 and its output is rounded to bf16.
 
 The ternary contraction is an fp32 matmul of integer-valued tensors: every
 product and partial sum is an integer below 2^24, so it is exact in any order.
+The square root and the divisions of the norm and the activation scale use
+NumPy's IEEE operations: torch's CPU sqrt and its Python-scalar division are
+not correctly rounded for every input, the kernels' __fsqrt_rn / __fdiv_rn are.
+
+Pinned to the installed HF BitNet forward (tests/test_hf_pin.py): wiring with
+the activation quantiser off on both sides, planted wiring mistakes rejected,
+RoPE against HF's apply_rotary_pos_emb, norm and ActQuant piece by piece.
 """
 
 from __future__ import annotations
@@ -29,26 +36,48 @@ def bf(x: torch.Tensor) -> torch.Tensor:
     return x.to(torch.bfloat16).to(torch.float32)
 
 
+def _ieee_rsqrt(var: torch.Tensor, eps: float) -> torch.Tensor:
+    """fp32 1 / sqrt(var + eps) with IEEE-rounded sqrt and division (NumPy).
+    torch's CPU sqrt and its Python-scalar division are not correctly rounded
+    for every input (measured: ~0.6% and ~25% of random float32 inputs differ
+    by one ulp), while the kernels use __fsqrt_rn / __fdiv_rn."""
+    v = var.numpy().astype(np.float32) + np.float32(eps)
+    return torch.from_numpy(np.float32(1.0) / np.sqrt(v))
+
+
 def rmsnorm(x: torch.Tensor, gamma: torch.Tensor | None, eps: float) -> torch.Tensor:
     if gamma is None:
         return x
     k = x.shape[-1]
     ss = (x.double() ** 2).sum(-1, keepdim=True)
     var = (ss / k).float()
-    r = 1.0 / torch.sqrt(var + torch.tensor(eps, dtype=torch.float32))
+    r = _ieee_rsqrt(var, eps)
     return bf(gamma * bf(x * r))
 
 
 def bitlinear(x: torch.Tensor, gamma: torch.Tensor | None, eps: float, w: torch.Tensor,
-              col_scale: torch.Tensor) -> torch.Tensor:
+              col_scale: torch.Tensor, act_quant: bool = True) -> torch.Tensor:
     """Fused BitLinear on float32 tensors holding bf16 / ternary values.
-    Returns bf16-valued float32 y = bf16(acc * (w_scale / s))."""
+    Returns bf16-valued float32 y = bf16(acc * (w_scale / s)).
+
+    act_quant=False skips the int8 activation quantiser (y = bf16((a @ W^T) *
+    w_scale) in float32): only the check of the decoder's wiring against the HF
+    forward uses it, where the quantiser would turn bf16-vs-float32 rounding
+    differences into code flips that mask what is compared."""
     a = rmsnorm(x, gamma, eps)
+    wf = w if w.dtype == torch.float32 else w.float()  # int8-stored codes widen exactly
+    if not act_quant:
+        return bf((a @ wf.t()) * col_scale[None, :])
     amax = a.abs().amax(-1).clamp_min(torch.tensor(1e-5, dtype=torch.float32))
-    s = torch.tensor(127.0, dtype=torch.float32) / amax
+    s = torch.from_numpy(np.float32(127.0) / amax.numpy())  # IEEE division (see _ieee_rsqrt)
     q = torch.round(a * s[:, None]).clamp(-128, 127)
-    acc = q @ w.t()
+    acc = q @ wf.t()
     return bf(acc * (col_scale[None, :] / s[:, None]))
+
+
+def relu2_mul(g: torch.Tensor, u: torch.Tensor) -> torch.Tensor:
+    """HF BitNetMLP act_fn "relu2" (ReLU then square) times up, in bf16 steps."""
+    return bf(torch.where(g > 0, bf(g * g), torch.zeros_like(g)) * u)
 
 
 def rope_tables(head_dim: int, max_len: int, theta: float) -> tuple[torch.Tensor, torch.Tensor]:
@@ -108,8 +137,18 @@ def _tern(w, quant: str = "numpy") -> tuple[torch.Tensor, float]:
 class OracleBitNet:
     """Greedy-decoding BitNet on the CPU from a (converted-key) state dict."""
 
-    def __init__(self, config, state_dict, max_len: int = 2048, quant: str = "numpy"):
+    def __init__(self, config, state_dict, max_len: int = 2048, quant: str = "numpy", compact: bool = False,
+                 act_quant: bool = True):
+        """compact: keep the ternary codes as int8 (a quarter of the memory of the
+        float32 codes; widened per use), for the full-depth 2B-4T-shaped model.
+        act_quant=False: BitLinears without the activation quantiser (see
+        bitlinear()); only for the wiring check against the HF forward."""
         self.cfg = config
+        self.act_quant = act_quant
+        # arithmetic of the attention's scores, softmax and weighted sum (the
+        # output is rounded to bf16 either way); float64 gives a second, equally
+        # valid reading of the fp32 attention, used to measure the noise floor
+        self.attn_dtype = torch.float32
         c = config
         self.d = c.head_dim
         self.nq, self.nkv = c.num_attention_heads, c.num_key_value_heads
@@ -128,6 +167,8 @@ class OracleBitNet:
             wg, sg = _tern(state_dict[p + "mlp.gate_proj.weight"], quant)
             wu, su = _tern(state_dict[p + "mlp.up_proj.weight"], quant)
             wd, sd = _tern(state_dict[p + "mlp.down_proj.weight"], quant)
+            if compact:
+                wq, wk, wv, wo, wg, wu, wd = (w.to(torch.int8) for w in (wq, wk, wv, wo, wg, wu, wd))
             s_qkv = torch.cat([torch.full((wq.shape[0],), sq), torch.full((wk.shape[0],), sk),
                                torch.full((wv.shape[0],), sv)]).float()
             self.layers.append(OracleLayer(
@@ -139,8 +180,8 @@ class OracleBitNet:
         self.cos, self.sin = rope_tables(self.d, max_len, c.rope_theta)
         self.max_len = max_len
 
-    def new_cache(self, batch: int) -> list[tuple[torch.Tensor, torch.Tensor]]:
-        shape = (batch, self.nkv, self.max_len, self.d)
+    def new_cache(self, batch: int, length: int | None = None) -> list[tuple[torch.Tensor, torch.Tensor]]:
+        shape = (batch, self.nkv, length or self.max_len, self.d)
         return [(torch.zeros(shape), torch.zeros(shape)) for _ in self.layers]
 
     def attention(self, qkv: torch.Tensor, pos: torch.Tensor, cache) -> torch.Tensor:
@@ -158,11 +199,12 @@ class OracleBitNet:
             p = int(pos[i])
             kc[i, :, p] = k[i]
             vc[i, :, p] = v[i]
-            keys, vals = kc[i, :, : p + 1], vc[i, :, : p + 1]           # [nkv, L, d]
-            qi = q[i].reshape(nkv, g, d)
+            dt = self.attn_dtype
+            keys, vals = kc[i, :, : p + 1].to(dt), vc[i, :, : p + 1].to(dt)  # [nkv, L, d]
+            qi = q[i].reshape(nkv, g, d).to(dt)
             sc = torch.einsum("hgd,hld->hgl", qi, keys) * (d ** -0.5)
             pr = torch.softmax(sc, dim=-1)
-            out[i] = torch.einsum("hgl,hld->hgd", pr, vals).reshape(nq, d)
+            out[i] = torch.einsum("hgl,hld->hgd", pr, vals).reshape(nq, d).float()
         return bf(out.reshape(b, nq * d))
 
     def prefill_attention(self, qkv: torch.Tensor, b: int, plen: int, cache) -> torch.Tensor:
@@ -182,12 +224,42 @@ class OracleBitNet:
         kc[:, :, :plen] = k.permute(0, 2, 1, 3)
         vc[:, :, :plen] = v.permute(0, 2, 1, 3)
         g = nq // nkv
-        qh = q.permute(0, 2, 1, 3).reshape(b, nkv, g, plen, d)
-        sc = torch.einsum("bhgpd,bhld->bhgpl", qh, kc[:, :, :plen]) * (d ** -0.5)
+        dt = self.attn_dtype
+        qh = q.permute(0, 2, 1, 3).reshape(b, nkv, g, plen, d).to(dt)
+        sc = torch.einsum("bhgpd,bhld->bhgpl", qh, kc[:, :, :plen].to(dt)) * (d ** -0.5)
         causal = torch.ones(plen, plen, dtype=torch.bool).triu(1)
         sc = sc.masked_fill(causal, float("-inf"))
-        o = torch.einsum("bhgpl,bhld->bhgpd", torch.softmax(sc, dim=-1), vc[:, :, :plen])
+        o = torch.einsum("bhgpl,bhld->bhgpd", torch.softmax(sc, dim=-1), vc[:, :, :plen].to(dt)).float()
         return bf(o.reshape(b, nq, plen, d).permute(0, 2, 1, 3).reshape(b * plen, nq * d))
+
+    def layer(self, i: int, h: torch.Tensor, cache, attend) -> torch.Tensor:
+        """Decoder layer i on hidden rows h (bf16-valued float32): input norm ->
+        QKV -> attention (`attend(qkv, cache)`) -> attn_sub_norm -> o_proj +
+        residual -> post-attention norm -> gate/up -> ReLU^2 * up ->
+        ffn_sub_norm -> down + residual (HF modeling_bitnet.py:232-261, reference
+        model/transformer.py:181-254)."""
+        L, aq = self.layers[i], self.act_quant
+        qkv = bitlinear(h, L.in_ln, self.eps, L.w_qkv, L.s_qkv, aq)
+        a = attend(qkv, cache)
+        h = bf(h + bitlinear(a, L.attn_ln, self.eps, L.w_o, L.s_o, aq))
+        n = rmsnorm(h, L.post_ln, self.eps)
+        g = bitlinear(n, None, self.eps, L.w_g, L.s_g, aq)
+        u = bitlinear(n, None, self.eps, L.w_u, L.s_u, aq)
+        mid = relu2_mul(g, u)
+        return bf(h + bitlinear(mid, L.ffn_ln, self.eps, L.w_d, L.s_d, aq))
+
+    def layer_prefill(self, i: int, h: torch.Tensor, b: int, plen: int, cache) -> torch.Tensor:
+        """Layer i over the prompt rows h [b*plen, H]; writes cache rows 0 .. plen-1."""
+        return self.layer(i, h, cache, lambda qkv, c: self.prefill_attention(qkv, b, plen, c))
+
+    def layer_step(self, i: int, h: torch.Tensor, pos: torch.Tensor, cache) -> torch.Tensor:
+        """Layer i for one decode token per sequence at positions pos; writes row pos."""
+        return self.layer(i, h, cache, lambda qkv, c: self.attention(qkv, pos, c))
+
+    def head(self, h: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        """Final norm, tied lm_head and greedy argmax: (ids, bf16-valued logits)."""
+        logits = bf(rmsnorm(h, self.norm, self.eps) @ self.lm_head.t())
+        return torch.argmax(logits, dim=-1).to(torch.int32), logits
 
     def prefill(self, prompts: np.ndarray, caches) -> tuple[torch.Tensor, torch.Tensor]:
         """All prompt tokens [B, L] in one batched pass (src/bitnet_tt/model/
@@ -195,18 +267,9 @@ class OracleBitNet:
         (first generated ids [B], bf16-valued logits of the last prompt tokens)."""
         b, plen = prompts.shape
         h = self.embed[torch.from_numpy(prompts.reshape(-1).astype(np.int64))]
-        for L, cache in zip(self.layers, caches):
-            qkv = bitlinear(h, L.in_ln, self.eps, L.w_qkv, L.s_qkv)
-            a = self.prefill_attention(qkv, b, plen, cache)
-            h = bf(h + bitlinear(a, L.attn_ln, self.eps, L.w_o, L.s_o))
-            n = rmsnorm(h, L.post_ln, self.eps)
-            g = bitlinear(n, None, self.eps, L.w_g, L.s_g)
-            u = bitlinear(n, None, self.eps, L.w_u, L.s_u)
-            mid = bf(torch.where(g > 0, bf(g * g), torch.zeros_like(g)) * u)
-            h = bf(h + bitlinear(mid, L.ffn_ln, self.eps, L.w_d, L.s_d))
-        last = h.reshape(b, plen, -1)[:, -1]
-        logits = bf(rmsnorm(last, self.norm, self.eps) @ self.lm_head.t())
-        return torch.argmax(logits, dim=-1).to(torch.int32), logits
+        for i, cache in enumerate(caches):
+            h = self.layer_prefill(i, h, b, plen, cache)
+        return self.head(h.reshape(b, plen, -1)[:, -1])
 
     def prefill_ragged(self, prompts: list[np.ndarray], caches) -> tuple[torch.Tensor, torch.Tensor]:
         """Prompts of different lengths: each sequence through prefill() on its
@@ -222,18 +285,9 @@ class OracleBitNet:
     def step(self, ids: torch.Tensor, pos: torch.Tensor, caches) -> tuple[torch.Tensor, torch.Tensor]:
         """One greedy decode step: (next ids [B], bf16-valued logits [B, V])."""
         h = self.embed[ids.long()]
-        for L, cache in zip(self.layers, caches):
-            qkv = bitlinear(h, L.in_ln, self.eps, L.w_qkv, L.s_qkv)
-            a = self.attention(qkv, pos, cache)
-            h = bf(h + bitlinear(a, L.attn_ln, self.eps, L.w_o, L.s_o))
-            n = rmsnorm(h, L.post_ln, self.eps)
-            g = bitlinear(n, None, self.eps, L.w_g, L.s_g)
-            u = bitlinear(n, None, self.eps, L.w_u, L.s_u)
-            mid = bf(torch.where(g > 0, bf(g * g), torch.zeros_like(g)) * u)
-            h = bf(h + bitlinear(mid, L.ffn_ln, self.eps, L.w_d, L.s_d))
-        normed = rmsnorm(h, self.norm, self.eps)
-        logits = bf(normed @ self.lm_head.t())
-        return torch.argmax(logits, dim=-1).to(torch.int32), logits
+        for i, cache in enumerate(caches):
+            h = self.layer_step(i, h, pos, cache)
+        return self.head(h)
 
     def generate(self, prompts: np.ndarray, max_new_tokens: int) -> tuple[np.ndarray, list[torch.Tensor]]:
         """Equal-length prompts [B, L]: prompt tokens go through the decode step one

@@ -14,6 +14,8 @@ import torch
 
 from oracle import bitlinear as ob
 from oracle import model as om
+from parity_rules import near_tie as _near_tie
+from parity_rules import within_logit_tol as _within_logit_tol
 
 pytestmark = pytest.mark.gpu
 
@@ -386,24 +388,6 @@ def test_linear_api_bit_exact(cuda):
     np.testing.assert_array_equal(y.float().cpu().numpy(), ref["y"])
     with pytest.raises(ValueError):
         Linear(640, 384, cuda, weight_dtype="bfp4")
-
-
-def _near_tie(logits: torch.Tensor) -> torch.Tensor:
-    top2 = torch.topk(logits, 2, dim=-1).values
-    ulp = 2.0 ** (torch.floor(torch.log2(top2[:, 0].abs().clamp_min(1e-30))) - 7)
-    return (top2[:, 0] - top2[:, 1]) <= 2 * ulp
-
-
-def _within_logit_tol(ref_row: torch.Tensor, dev_id: int) -> tuple[bool, str]:
-    """A greedy mismatch after decoding on a device's own KV cache: allowed when
-    the oracle logits of its token and of the device's token differ by less
-    than the logits tolerance (2e-2 of the row's largest magnitude) or by at
-    most 2 bf16 ulps."""
-    top = int(torch.argmax(ref_row))
-    gap = float(ref_row[top] - ref_row[dev_id])
-    scale = float(ref_row.abs().max())
-    ulp = 2.0 ** (np.floor(np.log2(max(abs(float(ref_row[top])), 1e-30))) - 7)
-    return gap <= max(2e-2 * scale, 2 * ulp), f"gap {gap:.4g}, row scale {scale:.4g}, ulp {ulp:.3g}"
 
 
 @pytest.mark.parametrize("batch", [4, 32])
