@@ -156,6 +156,15 @@ class Batch32Generator:
         # batched_prefill=False: every prompt token goes through the decode graph
         self.batched_prefill = True
         self.prefill_chunk_tokens = 65536  # ragged prompts: tokens per prefill pass (bounds its buffers)
+        # layer_probe(i, hidden): called with the hidden rows after the embedding
+        # (i = -1) and after each layer i, from the eager paths only (prefill
+        # passes, and decode steps with enable_trace=False); never inside a graph
+        # capture.  Parity tests use it to compare every layer with the oracle.
+        self.layer_probe = None
+
+    def _probe(self, i: int, hidden: torch.Tensor) -> None:
+        if self.layer_probe is not None and not torch.cuda.is_current_stream_capturing():
+            self.layer_probe(i, hidden)
 
     def set_context_limit(self, n: int) -> None:
         """Bound the positions the next steps reach (positions + 1 <= n).  The
@@ -193,6 +202,7 @@ class Batch32Generator:
         m, cfg = self.model, self.config
         b, eps = st.batch, cfg.rms_norm_eps
         m.embed_tokens.gather_into(st.ids, st.hidden)
+        self._probe(-1, st.hidden)
         if self.persistent:
             if st.plan is None:
                 st.plan = _lib.DecodePlan(m, st.hidden, st.qkv, st.attn, st.mid, st.positions, st.rope_cos,
@@ -200,7 +210,7 @@ class Batch32Generator:
             st.plan.run()
         # per layer: fused norm + act-quant + BitLinear calls (one launch each
         # below the ridge batch, act-quant + BitLinear above it) and the attention
-        for layer, cache in zip(m.layers, st.caches) if not self.persistent else ():
+        for i, (layer, cache) in enumerate(zip(m.layers, st.caches) if not self.persistent else ()):
             attn = layer.self_attn
             attn.qkv_proj.forward_fused(st.hidden, layer.input_layernorm.weight, eps, st.act_h, st.qkv)
             attn.decode_attention(st.qkv, st.positions, st.rope_cos, st.rope_sin, cache, st.attn, st.max_ctx,
@@ -211,6 +221,7 @@ class Batch32Generator:
                                                  st.mid)
             layer.mlp.down_proj.forward_fused(st.mid, layer.mlp.ffn_sub_norm.weight, eps, st.act_f, st.hidden,
                                               residual=st.hidden)
+            self._probe(i, st.hidden)
         _lib.rmsnorm(st.hidden, m.norm.weight, eps, st.normed)
         if self.vocab_head is None:
             m.lm_head_argmax(st.normed, st.argmax_ws, st.ids, st.logits, st.positions)
@@ -295,7 +306,8 @@ class Batch32Generator:
         pb = self.prefill_buffers
         pb.ids.copy_(torch.from_numpy(np.ascontiguousarray(table, dtype=np.int32).reshape(-1)))
         m.embed_tokens.gather_into(pb.ids, pb.hidden)
-        for layer, cache in zip(m.layers, st.caches):
+        self._probe(-1, pb.hidden)
+        for i, (layer, cache) in enumerate(zip(m.layers, st.caches)):
             attn = layer.self_attn
             _lib.act_quant(pb.hidden, layer.input_layernorm.weight, eps, pb.act_h)
             attn.qkv_proj.forward_into(pb.act_h, n, pb.qkv)
@@ -308,6 +320,7 @@ class Batch32Generator:
             layer.mlp.gate_up_proj.forward_into(pb.act_h, n, pb.mid)
             _lib.act_quant(pb.mid, layer.mlp.ffn_sub_norm.weight, eps, pb.act_f)
             layer.mlp.down_proj.forward_into(pb.act_f, n, pb.hidden, residual=pb.hidden)
+            self._probe(i, pb.hidden)
         last = pb.hidden.view(b, plen, -1)[:, plen - 1]  # row stride plen * hidden
         _lib.rmsnorm(last, m.norm.weight, eps, st.normed)
         st.positions.fill_(plen - 1)
@@ -352,8 +365,9 @@ class Batch32Generator:
             pb.ids[:n].copy_(torch.from_numpy(np.concatenate(prompts[a:e]).astype(np.int32)))
             hidden, qkv, q, attn_out, mid = pb.hidden[:n], pb.qkv[:n], pb.q[:n], pb.attn[:n], pb.mid[:n]
             m.embed_tokens.gather_into(pb.ids[:n], hidden)
+            self._probe(-1, hidden)
             lmax = int(glens.max())
-            for layer, cache in zip(m.layers, st.caches):
+            for i, (layer, cache) in enumerate(zip(m.layers, st.caches)):
                 at = layer.self_attn
                 kc, vc = cache.key_cache[a:e], cache.value_cache[a:e]
                 _lib.act_quant(hidden, layer.input_layernorm.weight, eps, pb.act_h)
@@ -366,6 +380,7 @@ class Batch32Generator:
                 layer.mlp.gate_up_proj.forward_into(pb.act_h, n, mid)
                 _lib.act_quant(mid, layer.mlp.ffn_sub_norm.weight, eps, pb.act_f)
                 layer.mlp.down_proj.forward_into(pb.act_f, n, hidden, residual=hidden)
+                self._probe(i, hidden)
             last[a:e].copy_(hidden.index_select(0, cu[1:].long() - 1))
         _lib.rmsnorm(last, m.norm.weight, eps, st.normed)
         st.positions.copy_(torch.tensor(lens, dtype=torch.int32) - 1)
