@@ -137,6 +137,10 @@ def _tern(w, quant: str = "numpy") -> tuple[torch.Tensor, float]:
 class OracleBitNet:
     """Greedy-decoding BitNet on the CPU from a (converted-key) state dict."""
 
+    # defaults for instances assembled field by field (attention-only checks)
+    act_quant = True
+    attn_dtype = torch.float32
+
     def __init__(self, config, state_dict, max_len: int = 2048, quant: str = "numpy", compact: bool = False,
                  act_quant: bool = True):
         """compact: keep the ternary codes as int8 (a quarter of the memory of the
