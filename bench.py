@@ -31,6 +31,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -124,6 +125,8 @@ def parse() -> argparse.Namespace:
     p.add_argument("--prefill-reps", type=int, default=3)
     p.add_argument("--decode-path", choices=["per-op", "persistent"], default="per-op",
                    help="per-op: 9 launches per layer; persistent: every layer in one launch")
+    p.add_argument("--clock-log", default=None,
+                   help="directory for the nvidia-smi clock samples (default: a temporary directory)")
     p.add_argument("--vocab-shard", action="store_true",
                    help="with N > 1: split the lm_head by vocabulary rows over the ranks (two NCCL gathers per step)")
     return p.parse_args()
@@ -146,10 +149,11 @@ class ClockSampler:
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index: int):
+    def __init__(self, gpu_index: int, log_dir: str | None = None):
         self.gpu = gpu_index
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_rank{gpu_index}.csv")
+        d = log_dir or os.path.join(tempfile.gettempdir(), f"bitnet_bench_{os.getpid()}")
+        self.path = os.path.join(d, f"clocks_rank{gpu_index}.csv")
 
     def __enter__(self):
         os.makedirs(os.path.dirname(self.path), exist_ok=True)
@@ -237,21 +241,52 @@ def model_config(args):
 # ---------------------------------------------------------------------------
 # CPU side: the oracle (restatement of the reference's CPU path)
 # ---------------------------------------------------------------------------
+def workload_prompts(args, cfg, rank: int = 0) -> np.ndarray:
+    """The prompt ids rank `rank` decodes in configs 1 and 2 (both arms use them)."""
+    rng = np.random.default_rng(args.seed * 1000 + rank)
+    return rng.integers(0, cfg.vocab_size, size=(args.batch, args.prompt_len))
+
+
+def workload_config(args, world: int, b: int, lens, c4: bool, parallelism: str) -> dict:
+    """The `config` object of the JSON line; identical in both arms apart from
+    `parallelism`."""
+    return {
+        "workload": (f"config4: {args.sequences} sequences split over {world} GPU(s), ragged contexts "
+                     f"U[128, 4096], {args.new_tokens} new tokens, bf16 KV cache {args.max_seq_len}, "
+                     "CUDA graph") if c4 else
+                    ("config1: batch-1 greedy decode, BitNet-2B-4T shape, 16-token prompt, 128 new "
+                     "tokens, CUDA graph") if args.workload == "config1" else
+                    ("config2: batch-32 greedy decode, BitNet-2B-4T shape, 64-token prompts, "
+                     "128 new tokens, bf16 KV cache 2048, CUDA graph"),
+        "batch_per_gpu": b, "global_batch": b * world,
+        "prompt_len": (f"ragged, rank 0 mean {float(np.mean(lens)):.0f}, max {int(np.max(lens))}" if c4
+                       else args.prompt_len),
+        "new_tokens": args.new_tokens, "layers": args.layers, "parallelism": parallelism,
+        "decode_path": args.decode_path,
+        "lm_head": f"vocab-sharded over {world} ranks (NCCL gathers)" if args.vocab_shard and world > 1
+        else "replicated",
+        "l2": "inputs larger than L2 (1.26 GB weights streamed per step)",
+    }
+
+
 def cpu_decode_sample(args, steps: int, budget_s: float | None = None, warm: int = 1) -> dict:
-    """Build the CPU oracle of the same model and time `steps` batch decode steps
-    (`warm` untimed steps first) at the prompt's context."""
+    """Build the CPU oracle of the same model, prefill the same prompts as the
+    GPU arm (rank 0's), then time `steps` batch decode steps (`warm` untimed
+    steps first) from the end of the prompts."""
     from bitnet_tt.utils.weights import synthetic_state_dict
     from oracle.model import OracleBitNet
 
     torch.set_num_threads(os.cpu_count() or 1)
     cfg = model_config(args)
     sd = synthetic_state_dict(cfg, args.seed, device="cpu")
-    ctx = args.prompt_len + args.new_tokens + max(1, warm) + 1
+    steps = min(steps, args.new_tokens)  # positions stay within the workload's generation length
+    ctx = args.prompt_len + max(1, warm) + steps + 1
     o = OracleBitNet(cfg, sd, max_len=ctx, quant="torch")
     b = args.batch
     caches = o.new_cache(b)
-    rng = np.random.default_rng(args.seed)
-    ids = torch.from_numpy(rng.integers(0, cfg.vocab_size, size=b).astype(np.int32))
+    t0 = time.perf_counter()
+    ids, _ = o.prefill(workload_prompts(args, cfg), caches)  # untimed: fills KV rows 0 .. prompt_len-1
+    prefill_s = time.perf_counter() - t0
     pos = torch.full((b,), args.prompt_len, dtype=torch.int32)
     for _ in range(max(1, warm)):  # untimed
         ids, _ = o.step(ids, pos, caches)
@@ -264,19 +299,21 @@ def cpu_decode_sample(args, steps: int, budget_s: float | None = None, warm: int
         if budget_s is not None and time.perf_counter() - t0 > budget_s:
             break
     dt = time.perf_counter() - t0
-    return {"tok_s": b * done / dt, "steps": done, "seconds": dt, "threads": torch.get_num_threads()}
+    return {"tok_s": b * done / dt, "steps": done, "seconds": dt, "threads": torch.get_num_threads(),
+            "prefill_s": prefill_s}
 
 
 def run_reference(args) -> None:
-    world, rank, _ = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")), 0
+    world, rank = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     want = max(1, args.steps)
     # the timed steps stop after --ref-budget-s seconds of CPU work (each step is ~1 s on 16 threads)
     r = cpu_decode_sample(args, want, budget_s=args.ref_budget_s, warm=args.warmup)
     sample = (f"{r['steps']} of {want} requested batch-{args.batch} decode steps of the full "
-              f"{args.layers}-layer model (context {args.prompt_len + args.warmup}..), CPU oracle, "
-              f"{r['threads']} threads, after {args.warmup} untimed steps")
+              f"{args.layers}-layer model on the CPU oracle ({r['threads']} threads), after a prefill of the "
+              f"same {args.batch} x {args.prompt_len} prompt ids as the B200 arm ({r['prefill_s']:.1f} s, untimed) "
+              f"and {args.warmup} untimed steps")
     c1 = args.workload == "config1"
     line = {
         "impl": "reference", "metric": METRIC_C1 if c1 else METRIC, "value": r["tok_s"], "unit": "tok/s",
@@ -284,12 +321,7 @@ def run_reference(args) -> None:
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "int8xternary->int32 (bf16 act/KV, bf16 lm_head)",
         "data": "synthetic (seeded random-init weights, uniform random prompt ids)",
-        "config": {"workload": ("config1: batch-1 greedy decode, BitNet-2B-4T shape, 16-token prompt, 128 new "
-                                "tokens") if c1 else
-                               ("config2: batch-32 greedy decode, BitNet-2B-4T shape, 64-token prompts, "
-                                "128 new tokens, bf16 KV cache 2048"),
-                   "batch_per_gpu": args.batch, "global_batch": args.batch, "prompt_len": args.prompt_len,
-                   "new_tokens": args.new_tokens, "layers": args.layers, "parallelism": "CPU oracle, rank 0"},
+        "config": workload_config(args, world, args.batch, [args.prompt_len], False, "CPU oracle, rank 0"),
         "cpu_baseline": {"value": r["tok_s"], "unit": "tok/s", "cores": r["threads"], "kind": "port",
                          "sample": sample},
         "e2e": {"value": r["tok_s"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -509,7 +541,7 @@ def run_config0(args) -> None:
         graph.replay()
     reps = max(1, args.steps // copies)
     torch.cuda.synchronize(dev)
-    with ClockSampler(0) as clocks:
+    with ClockSampler(0, args.clock_log) as clocks:
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         for _ in range(reps):
@@ -617,8 +649,7 @@ def run_b200(args) -> None:
     else:
         lens = np.full(b, args.prompt_len)
         gen.set_context_limit(args.prompt_len + args.new_tokens)  # positions cycle within it
-        rng = np.random.default_rng(args.seed * 1000 + rank)
-        prompts = rng.integers(0, cfg.vocab_size, size=(b, args.prompt_len))
+        prompts = workload_prompts(args, cfg, rank)
     torch.cuda.synchronize(device)
     t_pf = time.perf_counter()
     gen.prefill(prompts)
@@ -647,7 +678,7 @@ def run_b200(args) -> None:
     # ---- device-timed decode ------------------------------------------------
     barrier(world)
     torch.cuda.synchronize(device)
-    with ClockSampler(local) as clocks:
+    with ClockSampler(local, args.clock_log) as clocks:
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         for _ in range(args.steps):
@@ -694,7 +725,8 @@ def run_b200(args) -> None:
         r = cpu_decode_sample(args, args.cpu_baseline_steps)
         cpu = {"value": r["tok_s"], "unit": "tok/s", "cores": r["threads"], "kind": "port",
                "sample": f"{r['steps']} batch-{b} decode steps of the full {args.layers}-layer model on the CPU "
-                         f"oracle (context {args.prompt_len + 1}..), after 1 warm step"}
+                         f"oracle after a prefill of the same prompt ids ({r['prefill_s']:.1f} s, untimed) and "
+                         f"1 warm step (context {args.prompt_len + 1}..)"}
 
     if world > 1:
         import torch.distributed as dist
@@ -734,23 +766,8 @@ def run_b200(args) -> None:
         "vs_baseline": round(value / REF_SINGLE_USER_TOK_S, 2) if args.workload == "config1" else None,
         "dtype": "int8xternary->int32 (bf16 act/KV, bf16 lm_head)",
         "data": "synthetic (seeded random-init weights, uniform random prompt ids)",
-        "config": {"workload": (f"config4: {args.sequences} sequences split over {world} GPU(s), ragged contexts "
-                                f"U[128, 4096], {args.new_tokens} new tokens, bf16 KV cache {args.max_seq_len}, "
-                                "CUDA graph") if c4 else
-                               ("config1: batch-1 greedy decode, BitNet-2B-4T shape, 16-token prompt, 128 new "
-                                "tokens, CUDA graph") if args.workload == "config1" else
-                               ("config2: batch-32 greedy decode, BitNet-2B-4T shape, 64-token prompts, "
-                                "128 new tokens, bf16 KV cache 2048, CUDA graph"),
-                   "batch_per_gpu": b, "global_batch": b * world,
-                   "prompt_len": (f"ragged, rank 0 mean {lens.mean():.0f}, max {lens.max()}" if c4
-                                  else args.prompt_len),
-                   "prefill_s_rank0": round(t_pf, 2),
-                   "new_tokens": args.new_tokens, "layers": args.layers, "parallelism": f"dp{world} (batch split)",
-                   "decode_path": args.decode_path,
-                   "lm_head": f"vocab-sharded over {world} ranks (NCCL gathers)" if args.vocab_shard and world > 1
-                   else "replicated",
-                   "l2": "inputs larger than L2 (1.26 GB weights streamed per step)",
-                   "model_build_s": round(t_build, 1)},
+        "config": workload_config(args, world, b, lens, c4, f"dp{world} (batch split)"),
+        "timings": {"prefill_s_rank0": round(t_pf, 2), "model_build_s": round(t_build, 1)},
         "e2e": {"value": round(e2e_value, 1), "unit": "tok/s", "h2d_bytes_per_step": 4 * b,
                 "d2h_bytes_per_step": 4 * b},
         "gpu_launches": launches,
