@@ -11,9 +11,13 @@
 //   q_k    = clamp(rint(a_k * s), -128, 127)     half-to-even, as np.round / torch.round
 //   sum    = sum_k q_k                           (row_sum, used by the ternary epilogue)
 // Without gamma, a_k = x_k.  Every fp32 operation is an explicit _rn intrinsic so
-// the compiler cannot contract or reorder it; the fp64 sum of squares of bf16
-// values is exact for any summation order whenever the squares span less than
-// 2^37 in magnitude, so the codes do not depend on the reduction tree.
+// the compiler cannot contract or reorder it.  A square of a bf16 value has at
+// most 16 significant bits, so the fp64 sum of K of them is exact in any order
+// when the largest square is at most 2^(37 - ceil(log2 K)) times the smallest
+// nonzero one (|x| spanning 2^12 at K = 2560): the codes then cannot depend on
+// the reduction tree.  Beyond that span the sum may round, and two orders can
+// differ in the last bits of ss; var = fp32(ss / K) still agrees unless ss / K
+// lies within ~2^-29 (relative) of an fp32 rounding boundary.
 #pragma once
 #include "common.cuh"
 

@@ -190,3 +190,26 @@ def test_hf_checkpoint_round_trip(tmp_path):
               "vocab_size", "rms_norm_eps", "rope_theta"):
         assert getattr(cfg2, f) == getattr(cfg, f), f
     assert "layers.1.self_attn.attn_sub_norm.weight" in sd2 and "embed_tokens.weight" in sd2
+
+
+@pytest.mark.filterwarnings("ignore:overflow encountered")
+@pytest.mark.parametrize("k", [2560, 6912])
+def test_sum_of_squares_exact_span_and_extreme_rows(k):
+    """Rows inside the documented span give the same fp64 sum of squares in every
+    order (equal to the exact sum); rows far outside it may not, which is where
+    device and oracle could stop agreeing bit for bit.  The oracle's quantiser
+    stays finite on every extreme row (overflowing and underflowing variances)."""
+    import math
+
+    from extreme_rows import ROW_NAMES, extreme_rows, span_is_exact, var_orders
+
+    rows = extreme_rows(k, seed=k)
+    for name, row in zip(ROW_NAMES, rows):
+        sq = row.astype(np.float64) ** 2
+        if span_is_exact(row):
+            assert float(np.sum(sq)) == math.fsum(sq.tolist()), name
+            assert len(set(var_orders(row).values())) == 1, name
+    assert span_is_exact(rows[1]) and not span_is_exact(rows[2])
+    ref = ob.bitlinear(rows, np.ones(k, np.float32), 1e-5, np.zeros((1, k), np.int8))
+    assert np.isfinite(ref["normed"]).all() and np.isfinite(ref["s"]).all()
+    assert not ref["q"][4].any()  # var overflows fp32: r = 0, every normalised value 0, codes 0

@@ -303,3 +303,29 @@ def test_bounded_wait_gives_up_with_a_status_and_the_context_stays_usable(cuda):
     ref = ob.bitlinear(f32(x), None, 1e-5, np.zeros((1, 256), np.int8))
     np.testing.assert_array_equal(q, ref["q"])
     assert L.last_device_status() == (0, 0)
+
+
+@pytest.mark.filterwarnings("ignore:overflow encountered")
+@pytest.mark.parametrize("k", [2560, 6912])
+def test_act_quant_extreme_dynamic_range_rows(cuda, k):
+    """Rows at the edges of the bf16 range (1e-20 mixed with 1e17, magnitudes over
+    2^-30 .. 2^30, an overflowing variance, subnormals only, ...): the kernel's
+    codes, scales, row sums and normalised values equal the oracle's wherever the
+    fp32 variance does not depend on the order of the fp64 sum of squares (every
+    row here; a row whose variance did would be reported, not asserted)."""
+    from extreme_rows import ROW_NAMES, extreme_rows, var_orders
+
+    rows = extreme_rows(k, seed=k)
+    gamma = (1 + 0.1 * rand_bf16((k,), seed=k + 1).float()).to(torch.bfloat16)
+    x = torch.from_numpy(rows).to(torch.bfloat16)
+    q, s, rsum, normed = run_act_quant(x, gamma, 1e-5, cuda)
+    ref = ob.bitlinear(rows, f32(gamma), 1e-5, np.zeros((1, k), np.int8))
+    order_dependent = []
+    for i, name in enumerate(ROW_NAMES):
+        if len(set(var_orders(rows[i]).values())) != 1:
+            order_dependent.append(name)
+            continue
+        np.testing.assert_array_equal(normed[i], ref["normed"][i], err_msg=name)
+        np.testing.assert_array_equal(q[i], ref["q"][i], err_msg=name)
+        assert s[i] == ref["s"][i] and rsum[i] == ref["row_sum"][i], name
+    assert not order_dependent, f"rows whose fp32 variance depends on the summation order: {order_dependent}"
