@@ -280,6 +280,128 @@ act_quant_vec_kernel(const uint16_t* __restrict__ x, int M, int K, int ldx, cons
                 threadIdx.x);
 }
 
+// Decode path (few rows): one CTA per token row with one thread per C chunks of
+// 8 elements (blockDim = 32 * ceil(Kp / 8 / C / 32): 320 threads at K = 2560,
+// 864 at K = 6912 with C = 1), so no thread carries empty chunks through the
+// fp64 squares, the normalisation and the quantisation.  Every thread keeps
+// its chunks in registers; the three reductions (fp64 sum of squares, max,
+// integer sum) take one barrier each, with separate scratch so none is
+// overwritten before every thread has read it.  Same arithmetic as aq_row_vec
+// (bit-identical codes, scales, sums and normalised values).  Needs K % 8 == 0,
+// 16-byte aligned rows (ldx % 8 == 0) and gamma, and Kp / 8 <= 1024 * C.
+template <int C>
+__global__ void __launch_bounds__(1024)
+act_quant_row_kernel(const uint16_t* __restrict__ x, int M, int K, int ldx, const uint16_t* __restrict__ gamma,
+                     float eps, int8_t* __restrict__ q, float* __restrict__ row_scale, int32_t* __restrict__ row_sum,
+                     uint16_t* __restrict__ normed_out, int T, int Kp) {
+  __shared__ double red_d[32];
+  __shared__ float red_f[32];
+  __shared__ int red_i[32];
+  pdl_trigger();
+  const int t = threadIdx.x, nt = blockDim.x, nw = nt >> 5, lane = t & 31, warp = t >> 5;
+  const int KC8 = K >> 3;
+  uint4 gr[C];
+#pragma unroll
+  for (int c = 0; c < C; ++c) {
+    const int ch = t + c * nt;
+    gr[c] = (gamma != nullptr && ch < KC8) ? reinterpret_cast<const uint4*>(gamma)[ch] : make_uint4(0, 0, 0, 0);
+  }
+  pdl_wait();
+  const int m = blockIdx.x;
+  const bool valid = m < M;
+  uint4 xr[C];
+#pragma unroll
+  for (int c = 0; c < C; ++c) {
+    const int ch = t + c * nt;
+    xr[c] = (valid && ch < KC8) ? reinterpret_cast<const uint4*>(x + (size_t)m * ldx)[ch] : make_uint4(0, 0, 0, 0);
+  }
+  if (gamma != nullptr) {
+    double ss0 = 0.0, ss1 = 0.0;  // two independent chains (exact in any order within the span condition)
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+      float f[8];
+      aq_unpack8(xr[c], f);
+#pragma unroll
+      for (int e = 0; e < 8; e += 2) {
+        ss0 = fma((double)f[e], (double)f[e], ss0);
+        ss1 = fma((double)f[e + 1], (double)f[e + 1], ss1);
+      }
+    }
+    double ss = ss0 + ss1;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0) red_d[warp] = ss;
+    __syncthreads();
+    ss = red_d[0];
+    for (int i = 1; i < nw; ++i) ss += red_d[i];
+    const float var = __double2float_rn(__ddiv_rn(ss, (double)K));
+    const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+      float f[8], g[8];
+      aq_unpack8(xr[c], f);
+      aq_unpack8(gr[c], g);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) f[e] = round_bf16(__fmul_rn(g[e], round_bf16(__fmul_rn(f[e], r))));
+      xr[c] = aq_pack8(f);
+    }
+  }
+  if (normed_out != nullptr && valid) {
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+      const int ch = t + c * nt;
+      if (ch < KC8) reinterpret_cast<uint4*>(normed_out + (size_t)m * K)[ch] = xr[c];
+    }
+  }
+  if (q == nullptr) return;
+  float amax = 0.f;
+#pragma unroll
+  for (int c = 0; c < C; ++c) {
+    float f[8];
+    aq_unpack8(xr[c], f);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(f[e]));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  if (lane == 0) red_f[warp] = amax;
+  __syncthreads();
+  amax = red_f[0];
+  for (int i = 1; i < nw; ++i) amax = fmaxf(amax, red_f[i]);
+  amax = fmaxf(amax, 1e-5f);
+  const float s = __fdiv_rn(127.0f, amax);
+  int qsum = 0;
+#pragma unroll
+  for (int c = 0; c < C; ++c) {
+    const int ch = t + c * nt;
+    if (ch * 8 < Kp) {  // chunks past K (up to Kp) are written as zeros
+      float f[8];
+      aq_unpack8(xr[c], f);
+      uint32_t lo = 0, hi = 0;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        int qi = 0;
+        if (valid && ch < KC8) qi = max(-128, min(127, __float2int_rn(__fmul_rn(f[e], s))));
+        qsum += qi;
+        if (e < 4)
+          lo |= ((uint32_t)(qi & 0xFF)) << (8 * e);
+        else
+          hi |= ((uint32_t)(qi & 0xFF)) << (8 * (e - 4));
+      }
+      *reinterpret_cast<uint2*>(q + alayout_offset(m, ch * 8, T, Kp)) = make_uint2(lo, hi);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) qsum += __shfl_xor_sync(0xffffffffu, qsum, o);
+  if (lane == 0) red_i[warp] = qsum;
+  __syncthreads();
+  if (t == 0) {
+    for (int i = 1; i < nw; ++i) qsum += red_i[i];
+    row_scale[m] = valid ? s : 1.0f;
+    row_sum[m] = qsum;
+  }
+}
+
 // Many-row path (prefill): one warp per token row, 8 rows per CTA, every
 // reduction a warp shuffle (no block barrier).  Lane l keeps chunks
 // l, l + 32, ... (up to MAXC of 8 elements) in registers.  Same results as

@@ -427,6 +427,16 @@ int bitnet_act_quant(const void* x, int M, int K, int ldx, const void* gamma, fl
     return launch(k, dim3(rows / 8), dim3(256), 0, stream, 1, (const uint16_t*)x, M, K, ldx, (const uint16_t*)gamma,
                   eps, q, row_scale, row_sum, (uint16_t*)normed_out, act_tile_of(M), Kp);
   }
+  // few rows: one CTA per row, one thread per chunk of 8 (two or four chunks
+  // per thread for rows longer than 8192)
+  if (vec_ok && Kp / 8 <= 4 * 1024) {
+    const int chunks = Kp / 8;
+    const int C = chunks <= 1024 ? 1 : (chunks <= 2048 ? 2 : 4);
+    const int threads = ((chunks + C - 1) / C + 31) / 32 * 32;
+    auto k = C == 1 ? act_quant_row_kernel<1> : (C == 2 ? act_quant_row_kernel<2> : act_quant_row_kernel<4>);
+    return launch(k, dim3(rows), dim3(threads), 0, stream, 1, (const uint16_t*)x, M, K, ldx, (const uint16_t*)gamma,
+                  eps, q, row_scale, row_sum, (uint16_t*)normed_out, act_tile_of(M), Kp);
+  }
   if (vec_ok && Kp <= 8 * AQ_THREADS * AQ_MAXC)
     return launch(act_quant_vec_kernel, dim3(rows), dim3(AQ_THREADS), 0, stream, 1, (const uint16_t*)x, M, K, ldx,
                   (const uint16_t*)gamma, eps, q, row_scale, row_sum, (uint16_t*)normed_out, act_tile_of(M), Kp);
