@@ -50,7 +50,8 @@ constexpr int TC_PRODUCER_WARP = 11;
 // sub-partition then admits only one CTA per SM)
 constexpr int TC_THREADS = 12 * 32;
 constexpr int TC_EPI_THREADS = TC_UNPACK_WARPS * 32;
-constexpr int TC_STAGE_CHUNKS = 4;  // 4 x 64 = 256 K positions per stage (the most; TcParams::sc)
+constexpr int TC_STAGE_CHUNKS = 4;  // 4 x 64 = 256 K positions per stage (prefill; TcParams::sc)
+constexpr int TC_MAX_STAGE_CHUNKS = 8;  // decode stages: up to 8 x 64 = 512 K positions
 constexpr int TC_MAX_SLOTS = 16;
 constexpr int TC_MAX_NBUF = 8;      // A buffers in TMEM (64 columns each)
 constexpr int TC_TMEM_COLS = 512;       // one CTA per SM; 256 when two CTAs share an SM
@@ -72,7 +73,7 @@ struct TcParams {
   int split;
   int nbuf;  // A buffers in TMEM
   int tmem_cols;  // 512 (one CTA per SM) or 256 (two)
-  int sc;         // K chunks of 64 per stage: 4, or 2 for 256-token tiles (twice the stages in flight)
+  int sc;         // K chunks of 64 per stage: 4 (prefill), up to TC_MAX_STAGE_CHUNKS at decode
 };
 
 __host__ __device__ __forceinline__ int tc_slot_bytes(int T, int sc = TC_STAGE_CHUNKS) { return sc * 2048 + sc * 64 * T; }
@@ -278,8 +279,13 @@ __global__ void __launch_bounds__(TC_THREADS, 2) bitlinear_tc_kernel(const TcPar
           mma_i8_ts(d, a_base + kk * 8, bdesc, idesc, first ? 0u : 1u);
           first = false;
         }
-        tc_commit(&ctrl->a_empty[b]);
-        tc_commit(&ctrl->slot_free[slot]);
+        // A tcgen05.commit holds its issuing thread for about a microsecond
+        // (measured on B200: a commit every 8 MMAs turns 43 ns per MMA into
+        // 166 ns), so an A buffer or ring slot is released only when a later
+        // stage of this CTA reuses it; every wait on a_empty / slot_free is
+        // for exactly those stages.
+        if (s + NB < nstages) tc_commit(&ctrl->a_empty[b]);
+        if (s + nslot < nstages) tc_commit(&ctrl->slot_free[slot]);
       }
       tc_commit(&ctrl->d_final);
     }

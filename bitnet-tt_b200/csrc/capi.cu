@@ -264,12 +264,28 @@ int dispatch_tc(TcParams p, int ntile_n, int ntile_m, bitnet_stream_t st, const 
   }
   // K chunks per stage.  Halving the stage for 256-token tiles (twice the
   // stages in flight) was measured slower: a stage's copies cost ~0.7 us of
-  // fixed time whatever their size, so fewer, larger stages win.
-  const int sc = TC_STAGE_CHUNKS;
+  // fixed time whatever their size, so fewer, larger stages win.  At decode
+  // (T <= 64) each stage also costs the MMA issuers ~0.7 us of barrier waits
+  // and fences whatever its size (measured on B200 with per-stage timestamps),
+  // so the CTA's K range is cut into as few stages of at most
+  // TC_MAX_STAGE_CHUNKS chunks as possible, balanced, that still leave an A
+  // buffer per stage (up to two) in the tensor memory of the CTAs-per-SM the
+  // grid needs.
+  int sc = TC_STAGE_CHUNKS;
+  const int chunks_max = (p.KC + split - 1) / split;
+  if (p.T <= 64) {
+    const bool two_per_sm = (long)tiles * split > dev.sms;
+    for (int nst = (chunks_max + TC_MAX_STAGE_CHUNKS - 1) / TC_MAX_STAGE_CHUNKS; nst <= chunks_max; ++nst) {
+      sc = (chunks_max + nst - 1) / nst;
+      const int stages = (chunks_max + sc - 1) / sc;
+      if (tc_nbuf(p.T, two_per_sm ? 256 : TC_TMEM_COLS, sc) >= std::min(2, stages)) break;
+    }
+  }
+  const int stages_max = (chunks_max + sc - 1) / sc;
   int cols = TC_TMEM_COLS;
   // two CTAs per SM, when both the tensor memory and the shared memory of the
-  // smallest ring fit twice
-  if ((long)tiles * split > dev.sms && tc_nbuf(p.T, 256, sc) >= 2 &&
+  // smallest ring fit twice (with an A buffer per stage, up to two)
+  if ((long)tiles * split > dev.sms && tc_nbuf(p.T, 256, sc) >= std::min(2, stages_max) &&
       tc_smem_bytes(p.T, 2, split, 256, sc) <= tc_smem_limit(256))
     cols = 256;
   if (split > 8 || split > p.KC) return BITNET_ERR_INVALID_ARGUMENT;
