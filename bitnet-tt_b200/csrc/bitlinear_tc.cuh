@@ -163,6 +163,10 @@ __global__ void __launch_bounds__(TC_THREADS, 2) bitlinear_tc_kernel(const TcPar
   // The next kernel may launch now: its CTAs can start their own weight
   // prefetch while this one runs; it waits for this grid before reading it.
   pdl_trigger();
+  // Every thread waits for the whole cluster here, at the start (the CTAs of
+  // a cluster are co-scheduled), so the barrier's latency overlaps the weight
+  // prefetch instead of delaying the partial-sum exchange after the MMAs.
+  if (split > 1) cluster_wait();
   const uint32_t tbase = ctrl->tmem_base;
   const uint32_t tmem_d = tbase + NB * acols;  // D_i at tmem_d + i * T
 
@@ -213,10 +217,19 @@ __global__ void __launch_bounds__(TC_THREADS, 2) bitlinear_tc_kernel(const TcPar
       bulk_g2s(ring + (size_t)s * slot_bytes + wslot_bytes, p.q + (size_t)mt * T * p.Kp + (size_t)kc_s * 64 * T,
                nch * 64 * T, &ctrl->x_full[s]);
     }
+    // Per-token scale factors (one IEEE division per token, done here while
+    // the MMAs run rather than after them): fac0 = w_scale / row_scale (the gate
+    // scale for RELU2_MUL), fac1 = up scale / row_scale.  fac0 assumes the
+    // tile's rows share one segment; the epilogue divides per element when
+    // they do not.
+    const float sc0 = (EPI == EPI_RELU2_MUL) ? p.seg.scale[0] : seg_scale_of(p.seg, nb * 128);
     for (int i = lane; i < T; i += 32) {
       const int mg = mt * T + i;
-      ctrl->scale[i] = p.row_scale[mg];
+      const float s_i = p.row_scale[mg];
+      ctrl->scale[i] = s_i;
       ctrl->rsum[i] = p.row_sum[mg];
+      ctrl->fac0[i] = __fdiv_rn(sc0, s_i);
+      if (EPI == EPI_RELU2_MUL) ctrl->fac1[i] = __fdiv_rn(p.seg.scale[1], s_i);
     }
     // Refills (only when the K range has more stages than the ring has slots).
     // Lane 0 waits for the slot; the warp stays converged, and a large
@@ -328,7 +341,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2) bitlinear_tc_kernel(const TcPar
   // Everybody waits for the last MMA of every issuer.
   if (nstages > 0) wait(&ctrl->d_final, 0, 205);
   tc_fence_after();
-  __syncthreads();  // scale / row-sum staging by the producer is visible too
+  __syncthreads();  // scale, row-sum and factor staging by the producer is visible too
   pdl_wait();       // (already satisfied) orders this thread's reads of residual after the predecessor
 
   // Per-token scale factors, one IEEE division per token instead of one per
@@ -338,13 +351,6 @@ __global__ void __launch_bounds__(TC_THREADS, 2) bitlinear_tc_kernel(const TcPar
   const int N = p.N;
   const int row_lo = nb * 128, row_hi = min(N, row_lo + 128) - 1;
   const bool seg_uniform = (EPI == EPI_RELU2_MUL) || seg_scale_of(p.seg, row_lo) == seg_scale_of(p.seg, row_hi);
-  {
-    const float sc0 = (EPI == EPI_RELU2_MUL) ? p.seg.scale[0] : seg_scale_of(p.seg, row_lo);
-    for (int m = tid; m < T; m += TC_THREADS) {
-      ctrl->fac0[m] = __fdiv_rn(sc0, ctrl->scale[m]);
-      if (EPI == EPI_RELU2_MUL) ctrl->fac1[m] = __fdiv_rn(p.seg.scale[1], ctrl->scale[m]);
-    }
-  }
   const int used_acc = min(NACC, 2 * (kc_end - kc_begin));
 
   if (split == 1) {
@@ -356,7 +362,6 @@ __global__ void __launch_bounds__(TC_THREADS, 2) bitlinear_tc_kernel(const TcPar
     // overlap (y and residual may be the same buffer, which keeps the compiler
     // from moving a load above an earlier store).
     uint16_t* st = reinterpret_cast<uint16_t*>(ring);  // [T][TC_ST_LD] bf16
-    __syncthreads();  // fac0 / fac1 visible
     if (!*abort_flag) {
       // all 12 warps: warp w reads TMEM lane quarter w % 4 (the rows it may
       // access) and every third 16-token chunk
@@ -482,21 +487,24 @@ __global__ void __launch_bounds__(TC_THREADS, 2) bitlinear_tc_kernel(const TcPar
   const int ldr = tc_ldr(T, split);
   int* recv = reinterpret_cast<int*>(split > 1 ? ring + (size_t)nslot * slot_bytes : ring);
   int* stage = recv + (size_t)split * 128 * ldr;
-  if (split > 1) cluster_wait();  // every CTA of the cluster has started
   if (warp < TC_UNPACK_WARPS && !*abort_flag) {
     const int quarter = warp & 3, half = warp >> 2;
     const int row = quarter * 32 + lane;
     const uint32_t lanes = (uint32_t)(quarter * 32) << 16;
     for (int c = half * 16; c < T; c += 32) {
-      uint32_t sum[16];
+      // every accumulator's chunk in flight at once, one wait
+      uint32_t sum[16], v1[16], v2[16];
       tmem_ld16(tmem_d + lanes + c, sum);
+      if (used_acc > 1) tmem_ld16(tmem_d + lanes + T + c, v1);
+      if (used_acc > 2) tmem_ld16(tmem_d + lanes + 2 * T + c, v2);
       tmem_wait_ld();
-      for (int a = 1; a < used_acc; ++a) {
-        uint32_t v[16];
-        tmem_ld16(tmem_d + lanes + a * T + c, v);
-        tmem_wait_ld();
+      if (used_acc > 1) {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) sum[j] += v[j];
+        for (int j = 0; j < 16; ++j) sum[j] += v1[j];
+      }
+      if (used_acc > 2) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) sum[j] += v2[j];
       }
       int owner = c / tok_cap;  // one division per 16 tokens
       int obeg = owner * tok_cap;
@@ -518,6 +526,20 @@ __global__ void __launch_bounds__(TC_THREADS, 2) bitlinear_tc_kernel(const TcPar
   fence_proxy_async_smem();  // the staged partials are read by bulk copies
   tc_fence_before();
   __syncthreads();
+  const int m_begin = cr * tok_cap, m_end = min(T, m_begin + tok_cap);
+  // Residual-add owners read their first batch of residual values now, so the
+  // L2 round trip overlaps the wait for the peers' partials (the residual is
+  // final: this thread has passed griddepcontrol.wait, and every output
+  // element is read and then written by the one thread that owns it).
+  uint16_t res_pre[4] = {0, 0, 0, 0};
+  if (EPI == EPI_RESIDUAL_ADD && tid < TC_EPI_THREADS && !*abort_flag) {
+    const int n = nb * 128 + (tid & 127), m0 = m_begin + (tid >> 7);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int m = m0 + 2 * u, mg = mt * T + m;
+      if (m < m_end && n < p.N && mg < p.M) res_pre[u] = p.residual[(size_t)mg * p.N + n];
+    }
+  }
   if (split > 1) {
     if (tid < split && tid != cr && !*abort_flag) {
       const uint32_t dst = mapa_shared(smem_u32(recv + (size_t)cr * 128 * ldr), (uint32_t)tid);
@@ -531,7 +553,6 @@ __global__ void __launch_bounds__(TC_THREADS, 2) bitlinear_tc_kernel(const TcPar
   }
 
   const bool aborted = *abort_flag != 0;
-  const int m_begin = cr * tok_cap, m_end = min(T, m_begin + tok_cap);
   if (!aborted && tid < TC_EPI_THREADS) {
     if (EPI == EPI_RELU2_MUL) {
       const int pr = tid & 63;   // pair within the tile
@@ -575,10 +596,12 @@ __global__ void __launch_bounds__(TC_THREADS, 2) bitlinear_tc_kernel(const TcPar
       for (int m0 = m_begin + part; m0 < m_end; m0 += 8) {
         uint16_t res[4];
         if (EPI == EPI_RESIDUAL_ADD) {
+          const bool first = m0 == m_begin + part;  // prefetched before the partials arrived
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
             const int m = m0 + 2 * u, mg = mt * T + m;
-            res[u] = (m < m_end && row_ok && mg < p.M) ? p.residual[(size_t)mg * N + n] : (uint16_t)0;
+            res[u] = first ? res_pre[u]
+                           : ((m < m_end && row_ok && mg < p.M) ? p.residual[(size_t)mg * N + n] : (uint16_t)0);
           }
         }
 #pragma unroll
