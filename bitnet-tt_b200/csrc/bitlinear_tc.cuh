@@ -78,11 +78,16 @@ struct TcParams {
 
 __host__ __device__ __forceinline__ int tc_slot_bytes(int T, int sc = TC_STAGE_CHUNKS) { return sc * 2048 + sc * 64 * T; }
 // K split: rank j of the cluster owns tokens [j * tok_cap, (j + 1) * tok_cap);
-// one CTA's partial sums for one owner are 128 rows x ldr int32 (ldr odd, so
-// the owner's column reads are free of bank conflicts).
+// one CTA's partial sums for one owner are tok_cap tokens x 128 rows int32,
+// token-major, so a warp (32 consecutive rows) writes and reads 128
+// contiguous bytes per token.
 __host__ __device__ __forceinline__ int tc_tok_cap(int T, int split) { return (T + split - 1) / split; }
-__host__ __device__ __forceinline__ int tc_ldr(int T, int split) { return tc_tok_cap(T, split) | 1; }
-__host__ __device__ __forceinline__ int tc_part_bytes(int T, int split) { return 128 * tc_ldr(T, split) * 4; }
+__host__ __device__ __forceinline__ int tc_part_bytes(int T, int split) { return 128 * tc_tok_cap(T, split) * 4; }
+// tokens owned by cluster rank r
+__host__ __device__ __forceinline__ int tc_tok_own(int T, int split, int r) {
+  const int cap = tc_tok_cap(T, split), b = r * cap, e = b + cap < T ? b + cap : T;
+  return e > b ? e - b : 0;
+}
 __host__ __device__ __forceinline__ int tc_nacc(int T) { return T <= 32 ? 3 : (T <= 64 ? 2 : 1); }
 // A buffers of sc chunks (16 * sc TMEM columns each) beside the accumulators
 __host__ __device__ __forceinline__ int tc_nbuf(int T, int cols = TC_TMEM_COLS, int sc = TC_STAGE_CHUNKS) {
@@ -146,7 +151,10 @@ __global__ void __launch_bounds__(TC_THREADS, 2) bitlinear_tc_kernel(const TcPar
     }
     mbar_init(&ctrl->d_final, NACC);
     mbar_init(&ctrl->recv_full, 1);
-    if (split > 1) mbar_arrive_expect_tx(&ctrl->recv_full, (uint32_t)((split - 1) * tc_part_bytes(T, split)));
+    // every peer sends 128 rows x 4 bytes for each token this CTA owns
+    if (split > 1)
+      mbar_arrive_expect_tx(&ctrl->recv_full,
+                            (uint32_t)((split - 1) * 128 * 4 * tc_tok_own(T, split, (int)cluster_ctarank())));
     ctrl->abort_flag = 0;
     fence_mbar_init();
   }
@@ -477,20 +485,21 @@ __global__ void __launch_bounds__(TC_THREADS, 2) bitlinear_tc_kernel(const TcPar
   } else {
 
   // Partial D -> the owner of each token.  Rank j of the cluster owns tokens
-  // [j * tok_cap, min(T, (j + 1) * tok_cap)).  A CTA writes the partials of
-  // owner j into its own staging area and sends them with one bulk copy into
-  // owner j's receive slot (counted on the owner's recv_full barrier); its own
-  // share goes straight into its receive slot.  Scalar DSMEM stores cost ~0.2
-  // us each here; one bulk copy per owner replaces 16 of them per thread.
-  const int cr = (split > 1) ? (int)cluster_ctarank() : 0;
+  // [j * tok_cap, min(T, (j + 1) * tok_cap)) and holds one receive slot per
+  // source rank (tok_cap tokens x 128 rows, token-major).  Each thread sends
+  // its row's partials straight from registers: st.async into the owner's
+  // slot, counted on the owner's recv_full barrier, or a plain store for its
+  // own share.  A warp's store of one token covers 128 contiguous bytes.
+  const int cr = (int)cluster_ctarank();
   const int tok_cap = tc_tok_cap(T, split);
-  const int ldr = tc_ldr(T, split);
-  int* recv = reinterpret_cast<int*>(split > 1 ? ring + (size_t)nslot * slot_bytes : ring);
-  int* stage = recv + (size_t)split * 128 * ldr;
+  const int slot_ints = 128 * tok_cap;  // ints per receive slot
+  int* recv = reinterpret_cast<int*>(ring + (size_t)nslot * slot_bytes);
   if (warp < TC_UNPACK_WARPS && !*abort_flag) {
     const int quarter = warp & 3, half = warp >> 2;
     const int row = quarter * 32 + lane;
     const uint32_t lanes = (uint32_t)(quarter * 32) << 16;
+    int* own = recv + (size_t)cr * slot_ints + row;  // this rank's slot, at every owner
+    const uint32_t own_s = smem_u32(own), bar_s = smem_u32(&ctrl->recv_full);
     for (int c = half * 16; c < T; c += 32) {
       // every accumulator's chunk in flight at once, one wait
       uint32_t sum[16], v1[16], v2[16];
@@ -508,24 +517,25 @@ __global__ void __launch_bounds__(TC_THREADS, 2) bitlinear_tc_kernel(const TcPar
       }
       int owner = c / tok_cap;  // one division per 16 tokens
       int obeg = owner * tok_cap;
+      uint32_t dst = mapa_shared(own_s, (uint32_t)owner), dbar = mapa_shared(bar_s, (uint32_t)owner);
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
-        const int m = c + j;
+        const int m = c + j;  // < T: T is a multiple of 16
         if (m >= obeg + tok_cap) {
           ++owner;
           obeg += tok_cap;
+          dst = mapa_shared(own_s, (uint32_t)owner);
+          dbar = mapa_shared(bar_s, (uint32_t)owner);
         }
-        const int idx = row * ldr + (m - obeg);
         if (owner == cr)
-          recv[(size_t)cr * 128 * ldr + idx] = (int)sum[j];
+          own[(m - obeg) * 128] = (int)sum[j];
         else
-          stage[(size_t)owner * 128 * ldr + idx] = (int)sum[j];
+          st_async_s32(dst + (uint32_t)(m - obeg) * 512u, (int)sum[j], dbar);
       }
     }
   }
-  fence_proxy_async_smem();  // the staged partials are read by bulk copies
   tc_fence_before();
-  __syncthreads();
+  __syncthreads();  // this CTA's own share is visible to its epilogue threads
   const int m_begin = cr * tok_cap, m_end = min(T, m_begin + tok_cap);
   // Residual-add owners read their first batch of residual values now, so the
   // L2 round trip overlaps the wait for the peers' partials (the residual is
@@ -540,17 +550,9 @@ __global__ void __launch_bounds__(TC_THREADS, 2) bitlinear_tc_kernel(const TcPar
       if (m < m_end && n < p.N && mg < p.M) res_pre[u] = p.residual[(size_t)mg * p.N + n];
     }
   }
-  if (split > 1) {
-    if (tid < split && tid != cr && !*abort_flag) {
-      const uint32_t dst = mapa_shared(smem_u32(recv + (size_t)cr * 128 * ldr), (uint32_t)tid);
-      const uint32_t bar = mapa_shared(smem_u32(&ctrl->recv_full), (uint32_t)tid);
-      bulk_s2cluster(dst, stage + (size_t)tid * 128 * ldr, (uint32_t)tc_part_bytes(T, split), bar);
-      bulk_commit_group();
-    }
-    // Peers' copies land here even when this CTA gave up, so the wait does not
-    // depend on the abort flag (it is bounded like every wait).
-    if (!mbar_wait(&ctrl->recv_full, 0, 206)) *abort_flag = 1;
-  }
+  // Peers' stores land here even when this CTA gave up, so the wait does not
+  // depend on the abort flag (it is bounded like every wait).
+  if (!mbar_wait_cluster(&ctrl->recv_full, 0, 206)) *abort_flag = 1;
 
   const bool aborted = *abort_flag != 0;
   if (!aborted && tid < TC_EPI_THREADS) {
@@ -561,16 +563,16 @@ __global__ void __launch_bounds__(TC_THREADS, 2) bitlinear_tc_kernel(const TcPar
       const int ng = nb * 128 + g0, nu = ng + 32;
       const bool row_ok = nu < N;
       uint16_t* yb = p.y + nb * 64 + (g0 >> 6) * 32 + (g0 & 31);
-      const int* rg = recv + g0 * ldr - m_begin;
-      const int* ru = recv + (g0 + 32) * ldr - m_begin;
+      const int* rg = recv + g0 - m_begin * 128;
+      const int* ru = recv + (g0 + 32) - m_begin * 128;
       // Independent iterations: unrolled so their latency chains overlap.
 #pragma unroll 4
       for (int m = m_begin + part; m < m_end; m += 4) {
         const int mg = mt * T + m;
         int ag = -ctrl->rsum[m], au = ag;
         for (int j = 0; j < split; ++j) {
-          ag += rg[j * 128 * ldr + m];
-          au += ru[j * 128 * ldr + m];
+          ag += rg[j * slot_ints + m * 128];
+          au += ru[j * slot_ints + m * 128];
         }
         const float g = round_bf16(__fmul_rn((float)ag, ctrl->fac0[m]));
         const float u = round_bf16(__fmul_rn((float)au, ctrl->fac1[m]));
@@ -589,7 +591,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2) bitlinear_tc_kernel(const TcPar
       const int n = nb * 128 + row;
       const float wsc = seg_scale_of(p.seg, n);
       const bool row_ok = n < N;
-      const int* rr = recv + row * ldr - m_begin;
+      const int* rr = recv + row - m_begin * 128;
       // tokens in batches of 4 per thread; the batch's residuals are read before
       // any of its stores (y may be the residual buffer, which keeps the
       // compiler from moving a load above an earlier store)
@@ -610,7 +612,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2) bitlinear_tc_kernel(const TcPar
           if (m >= m_end) break;
           const int mg = mt * T + m;
           int a = -ctrl->rsum[m];
-          for (int j = 0; j < split; ++j) a += rr[j * 128 * ldr + m];
+          for (int j = 0; j < split; ++j) a += rr[j * slot_ints + m * 128];
           const float v = seg_uniform ? round_bf16(__fmul_rn((float)a, ctrl->fac0[m])) : scaled_bf16(a, wsc, ctrl->scale[m]);
           if (row_ok && mg < p.M) {
             const size_t o = (size_t)mg * N + n;
@@ -627,7 +629,6 @@ __global__ void __launch_bounds__(TC_THREADS, 2) bitlinear_tc_kernel(const TcPar
 
   }  // split > 1
 
-  if (split > 1 && tid < split) bulk_wait_group_read0();  // outgoing copies have read the staging area
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {

@@ -212,7 +212,7 @@ int dispatch_simt(const int8_t* q, const float* rs, const int32_t* rsum, int M, 
 size_t tc_smem_bytes(int T, int nslot, int split, int cols = TC_TMEM_COLS, int sc = TC_STAGE_CHUNKS) {
   const size_t ring = (size_t)nslot * tc_slot_bytes(T, sc);
   const size_t stage = (size_t)T * TC_ST_LD * 2;  // staged bf16 output tile (no K split)
-  const size_t recv = (size_t)2 * split * tc_part_bytes(T, split);  // receive slots + staging
+  const size_t recv = (size_t)split * tc_part_bytes(T, split);  // one receive slot per source rank
   size_t bytes = TC_CTRL_BYTES + (split > 1 ? ring + recv : (ring > stage ? ring : stage));
   const size_t floor_bytes = cols == 512 ? (size_t)116 * 1024 : (size_t)77 * 1024;
   return bytes < floor_bytes ? floor_bytes : bytes;

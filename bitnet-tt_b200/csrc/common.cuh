@@ -121,6 +121,31 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int si
   return true;
 }
 
+// Same wait with acquire at cluster scope: for data that other CTAs of the
+// cluster store with st.async (whose complete_tx releases at cluster scope).
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, int site) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try_wait_cluster(bar, parity)) {
+    if (clock64() - t0 > kSpinLimitCycles) {
+      record_error(DEV_ERR_TIMEOUT, site);
+      return false;
+    }
+  }
+  return true;
+}
+
 // Bulk asynchronous copy global -> this CTA's shared memory; completion is
 // signalled on `bar` as transaction bytes.  dst/src 16-byte aligned, bytes % 16 == 0.
 __device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
@@ -138,22 +163,6 @@ __device__ __forceinline__ void bulk_g2s_stream(void* smem_dst, const void* gsrc
           "r"(smem_u32(smem_dst)),
       "l"(gsrc), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
       : "memory");
-}
-// Bulk copy from this CTA's shared memory into another CTA of the cluster
-// (dst and mbar are shared::cluster addresses from mapa); completion is counted
-// as transaction bytes on the destination CTA's barrier.
-__device__ __forceinline__ void bulk_s2cluster(uint32_t dst_cluster, const void* src, uint32_t bytes,
-                                               uint32_t mbar_cluster) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-          dst_cluster),
-      "r"(smem_u32(src)), "r"(bytes), "r"(mbar_cluster)
-      : "memory");
-}
-__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-// Wait until the sources of this thread's committed bulk copies may be reused.
-__device__ __forceinline__ void bulk_wait_group_read0() {
-  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
 __device__ __forceinline__ uint64_t l2_policy_evict_first() {
   uint64_t p;
@@ -203,13 +212,14 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
   return r;
 }
-__device__ __forceinline__ void st_shared_cluster_s32(uint32_t addr, int v) {
-  asm volatile("st.shared::cluster.s32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
-}
-__device__ __forceinline__ int ld_shared_cluster_s32(uint32_t addr) {
-  int v;
-  asm volatile("ld.shared::cluster.s32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
-  return v;
+// Non-blocking 4-byte store into a cluster peer's shared memory (addr and mbar
+// are shared::cluster addresses of the same CTA, from mapa); the 4 bytes count
+// as transaction bytes on that CTA's barrier, whose completion makes them
+// visible to its waiters.
+__device__ __forceinline__ void st_async_s32(uint32_t addr_cluster, int v, uint32_t mbar_cluster) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.s32 [%0], %1, [%2];" ::"r"(addr_cluster),
+               "r"(v), "r"(mbar_cluster)
+               : "memory");
 }
 
 // ---------------------------------------------------------------------------
