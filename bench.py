@@ -57,12 +57,12 @@ NCU_TRAFFIC_BATCH = 32
 # K/V row is read once, so the traffic of a launch scales with the keys it reads.
 NCU_TRAFFIC_RATIO: dict[str, float] = {"attention": 359606784.0 / 353400320.0}
 NCU_TRAFFIC_BYTES: dict[str, float | None] = {
-    "bitlinear_qkv": 2610688.0,
-    "bitlinear_o": 1956096.0,
-    "bitlinear_gate_up": 9000192.0,
-    "bitlinear_down": 4880896.0,
-    "act_quant": 193792.0,
-    "lm_head": 659862528.0,
+    "bitlinear_qkv": 2611168.0,
+    "bitlinear_o": 1955136.0,
+    "bitlinear_gate_up": 8998432.0,
+    "bitlinear_down": 4879616.0,
+    "act_quant": 186432.0,
+    "lm_head": 657273280.0,
 }
 
 # Kernel classes timed by kernel_rooflines, grouped by the kernel (template
@@ -72,7 +72,7 @@ KERNEL_GROUPS = {
     "bitlinear_tc_kernel<residual> (o_proj, down)": ("bitlinear_o", "bitlinear_down"),
     "bitlinear_tc_kernel<relu2> (gate_up)": ("bitlinear_gate_up",),
     "bitlinear_tc_kernel<none> (qkv)": ("bitlinear_qkv",),
-    "act_quant_vec_kernel": ("act_quant",),
+    "act_quant_row_kernel": ("act_quant",),
     "gqa_decode_kernel": ("attention",),
     "lm_head (tile_hidden + lm_head_tc + argmax_reduce)": ("lm_head",),
     "decode_layers_kernel": ("decode_layers",),
@@ -589,7 +589,7 @@ def run_config0(args) -> None:
         "e2e": {"value": round(algo / (e2e_us * 1e-6) / 1e9, 2), "unit": "GB/s", "us_per_call": round(e2e_us, 2),
                 "h2d_bytes_per_step": 2 * m * k, "d2h_bytes_per_step": 2 * m * n},
         "gpu_launches": 2 * reps * copies,
-        "roofline": {"kernel": "act_quant_vec_kernel + bitlinear_tc_kernel<none>", "bound": "hbm",
+        "roofline": {"kernel": "act_quant_row_kernel + bitlinear_tc_kernel<none>", "bound": "hbm",
                      "achieved": round(gbs, 1), "peak": hbm_peak, "unit": "GB/s", "frac": round(gbs / hbm_peak, 4),
                      "traffic": None, "peak_kind": peak_kind},
         "cpu_baseline": {"value": round(algo / cpu_s / 1e9, 3), "unit": "GB/s", "cores": os.cpu_count(),
