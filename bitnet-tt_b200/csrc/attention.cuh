@@ -480,6 +480,25 @@ __global__ void __launch_bounds__(ATT_THREADS) gqa_decode_kernel(const AttnParam
     s_flag = 0;
     fence_mbar_init();
   }
+  // The K / V rows below the new position were written by earlier steps and
+  // have since left L2 (the step streams over a gigabyte of weights), so the
+  // unit asks for its rows while the previous kernel still runs.  A hint only:
+  // the position may not be final yet (it is read before griddepcontrol.wait),
+  // so it is clamped to the cache and the real loads come after the wait.
+  if (t == 0) {
+    int pos = p.positions[blockIdx.x];
+    pos = pos < 0 ? 0 : (pos >= p.max_len ? p.max_len - 1 : pos);
+    if (pos >= p.max_ctx) pos = p.max_ctx - 1;
+    int nparts = 1, span = pos + 1;
+    if (p.nsplit > 1) att_parts(pos + 1, p.nsplit, p.max_ctx, nparts, span);
+    const int r0 = (int)blockIdx.z * span, r1 = min(pos, r0 + span);  // row pos is written by this unit
+    if (r1 > r0) {
+      const size_t row0 = (((size_t)blockIdx.x * p.n_kv + blockIdx.y) * p.max_len + r0) * ATT_D;
+      const uint32_t bytes = (uint32_t)(r1 - r0) * ATT_D * 2;
+      prefetch_l2_bulk(p.k_cache + row0, bytes);
+      prefetch_l2_bulk(p.v_cache + row0, bytes);
+    }
+  }
   __syncthreads();
   pdl_wait();
   uint32_t tiles_done = 0;

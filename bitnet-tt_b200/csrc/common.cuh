@@ -164,6 +164,11 @@ __device__ __forceinline__ void bulk_g2s_stream(void* smem_dst, const void* gsrc
       "l"(gsrc), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
       : "memory");
 }
+// Hint: bring [gsrc, gsrc + bytes) into L2 (16-byte aligned, bytes a multiple
+// of 16).  No data moves into the CTA and nothing is waited on.
+__device__ __forceinline__ void prefetch_l2_bulk(const void* gsrc, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(gsrc), "r"(bytes) : "memory");
+}
 __device__ __forceinline__ uint64_t l2_policy_evict_first() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
