@@ -72,7 +72,18 @@ struct AttnParams {
   int* ws_count;    // [B * n_kv] arrival counters (zero between launches)
   float* ws_part;   // [B * n_kv * nsplit][2G + G * 128]
   uint16_t* out;
+  int prefetch;     // 1: units ask L2 for their K / V rows before griddepcontrol.wait
 };
+
+// K / V bytes a launch may touch, up to which the units' early L2 requests pay:
+// at config-2 contexts (32 sequences x 5 KV heads x 192 keys, 15.7 MB) they took
+// the decode step from 1520 to 1508 us; at config-4 contexts (hundreds of MB per
+// launch, more than L2 holds) they slowed the attention from 238 to 267 us per
+// launch (256 sequences) and from 72.7 to 81.5 us (64 sequences).
+constexpr size_t ATT_PREFETCH_MAX_BYTES = (size_t)32 << 20;
+inline int att_prefetch_pays(int B, int n_kv, int max_ctx) {
+  return (size_t)B * n_kv * max_ctx * ATT_D * 2 * 2 <= ATT_PREFETCH_MAX_BYTES ? 1 : 0;
+}
 
 __host__ __device__ __forceinline__ int att_part_floats(int G) { return 2 * G + G * ATT_D; }
 
@@ -485,7 +496,7 @@ __global__ void __launch_bounds__(ATT_THREADS) gqa_decode_kernel(const AttnParam
   // unit asks for its rows while the previous kernel still runs.  A hint only:
   // the position may not be final yet (it is read before griddepcontrol.wait),
   // so it is clamped to the cache and the real loads come after the wait.
-  if (t == 0) {
+  if (t == 0 && p.prefetch) {
     int pos = p.positions[blockIdx.x];
     pos = pos < 0 ? 0 : (pos >= p.max_len ? p.max_len - 1 : pos);
     if (pos >= p.max_ctx) pos = p.max_ctx - 1;

@@ -590,6 +590,7 @@ int bitnet_gqa_decode_attention(const void* qkv, int B, int n_heads, int n_kv_he
   p.max_len = max_len;
   p.max_ctx = max_ctx;
   p.nsplit = att_grid_splits(B, n_kv_heads, max_ctx);
+  p.prefetch = att_prefetch_pays(B, n_kv_heads, max_ctx);
   p.scale = scale;
   const size_t counters = ((size_t)B * n_kv_heads * sizeof(int) + 255) / 256 * 256;
   p.ws_count = ws_need > 0 ? (int*)workspace : nullptr;
@@ -1088,6 +1089,7 @@ extern "C" int bitnet_decode_plan_create(const bitnet_decode_desc_t* d, bitnet_d
   a.max_len = d->max_len;
   a.max_ctx = max_ctx;
   a.nsplit = att_grid_splits(B, NKV, max_ctx);
+  a.prefetch = 0;  // the persistent kernel has no launch to overlap
   a.scale = 1.0f / sqrtf((float)ATT_D);
   const size_t counters = ((size_t)B * NKV * sizeof(int) + 255) / 256 * 256;
   a.ws_count = att_ws > 0 ? (int*)d->attn_workspace : nullptr;
