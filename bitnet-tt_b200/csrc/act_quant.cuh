@@ -179,6 +179,36 @@ __device__ __forceinline__ uint4 aq_pack8(const float* f) {
   return o;
 }
 
+// RMSNorm of 8 values as HF computes it, bf16(gamma * bf16(x * r)), returned
+// packed as bf16 (the form every later step reads).  Each rounding handles two
+// values per conversion instruction.  Used by the one-row-per-CTA kernels
+// (decode), whose chain of dependent conversions it shortens: the decode step
+// went from 1507 to 1471 us.  The many-row kernels keep one conversion per
+// value: with these helpers they ran slower (68 -> 78 us at 16384 x 2560),
+// although the conversion pipe was 78% busy there.
+__device__ __forceinline__ uint4 aq_norm8(const uint4 xv, const uint4 gv, float r) {
+  float f[8], g[8];
+  aq_unpack8(xv, f);
+  aq_unpack8(gv, g);
+  uint32_t o[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const __nv_bfloat162 y = __floats2bfloat162_rn(__fmul_rn(f[2 * e], r), __fmul_rn(f[2 * e + 1], r));
+    const uint32_t yb = *reinterpret_cast<const uint32_t*>(&y);
+    const __nv_bfloat162 a = __floats2bfloat162_rn(__fmul_rn(g[2 * e], __uint_as_float(yb << 16)),
+                                                   __fmul_rn(g[2 * e + 1], __uint_as_float(yb & 0xFFFF0000u)));
+    o[e] = *reinterpret_cast<const uint32_t*>(&a);
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// rint(v), half to even, for |v| < 2^22 (the codes: |v| <= 127 plus rounding):
+// adding 1.5 * 2^23 leaves rint(v) in the low mantissa bits of the sum.  The
+// same result as __float2int_rn without the conversion pipe.
+__device__ __forceinline__ int aq_rint_small(float v) {
+  return __float_as_int(__fadd_rn(v, 12582912.0f)) - 0x4B400000;
+}
+
 // Row m (padded rows m >= M produce zero codes, scale 1, sum 0) on threads
 // t = 0..255.  The row stays in registers as packed bf16: the input is bf16 and
 // every normalised value is rounded to bf16, so repacking loses nothing.
@@ -210,12 +240,7 @@ __device__ void aq_row_vec(const uint16_t* __restrict__ x, int M, int K, int ldx
     const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
 #pragma unroll
     for (int c = 0; c < AQ_MAXC; ++c) {
-      float f[8], g[8];
-      aq_unpack8(xr[c], f);
-      aq_unpack8(gr[c], g);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) f[e] = round_bf16(__fmul_rn(g[e], round_bf16(__fmul_rn(f[e], r))));
-      xr[c] = aq_pack8(f);
+      xr[c] = aq_norm8(xr[c], gr[c], r);
     }
   }
   if (normed_out != nullptr && valid) {
@@ -247,7 +272,7 @@ __device__ void aq_row_vec(const uint16_t* __restrict__ x, int M, int K, int ldx
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
         int qi = 0;
-        if (valid && ch < KC8) qi = max(-128, min(127, __float2int_rn(__fmul_rn(f[e], s))));
+        if (valid && ch < KC8) qi = max(-128, min(127, aq_rint_small(__fmul_rn(f[e], s))));
         qsum += qi;
         if (e < 4)
           lo |= ((uint32_t)(qi & 0xFF)) << (8 * e);
@@ -338,12 +363,7 @@ act_quant_row_kernel(const uint16_t* __restrict__ x, int M, int K, int ldx, cons
     const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
 #pragma unroll
     for (int c = 0; c < C; ++c) {
-      float f[8], g[8];
-      aq_unpack8(xr[c], f);
-      aq_unpack8(gr[c], g);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) f[e] = round_bf16(__fmul_rn(g[e], round_bf16(__fmul_rn(f[e], r))));
-      xr[c] = aq_pack8(f);
+      xr[c] = aq_norm8(xr[c], gr[c], r);
     }
   }
   if (normed_out != nullptr && valid) {
@@ -381,7 +401,7 @@ act_quant_row_kernel(const uint16_t* __restrict__ x, int M, int K, int ldx, cons
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
         int qi = 0;
-        if (valid && ch < KC8) qi = max(-128, min(127, __float2int_rn(__fmul_rn(f[e], s))));
+        if (valid && ch < KC8) qi = max(-128, min(127, aq_rint_small(__fmul_rn(f[e], s))));
         qsum += qi;
         if (e < 4)
           lo |= ((uint32_t)(qi & 0xFF)) << (8 * e);
