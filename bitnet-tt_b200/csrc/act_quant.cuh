@@ -179,27 +179,48 @@ __device__ __forceinline__ uint4 aq_pack8(const float* f) {
   return o;
 }
 
+// Pairs of fp32 values in one 64-bit register, for the sm_100 .f32x2
+// arithmetic: one instruction performs two IEEE round-to-nearest operations,
+// each exactly as its scalar form.  Element 0 sits in the low half.
+__device__ __forceinline__ uint64_t f2_make(uint32_t lo_bits, uint32_t hi_bits) {
+  uint64_t d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "r"(lo_bits), "r"(hi_bits));
+  return d;
+}
+__device__ __forceinline__ void f2_split(uint64_t a, uint32_t& lo_bits, uint32_t& hi_bits) {
+  asm("mov.b64 {%0, %1}, %2;" : "=r"(lo_bits), "=r"(hi_bits) : "l"(a));
+}
+__device__ __forceinline__ uint64_t f2_splat(float v) { return f2_make(__float_as_uint(v), __float_as_uint(v)); }
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+// two packed bf16 values -> an fp32 pair (exact: a bf16 is the top half of an fp32)
+__device__ __forceinline__ uint64_t f2_from_bf2(uint32_t v) { return f2_make(v << 16, v & 0xFFFF0000u); }
+// fp32 pair -> two bf16 values, each rounded to nearest even, one conversion
+__device__ __forceinline__ uint32_t f2_to_bf2(uint64_t a) {
+  uint32_t lo, hi;
+  f2_split(a, lo, hi);
+  const __nv_bfloat162 b = __floats2bfloat162_rn(__uint_as_float(lo), __uint_as_float(hi));
+  return *reinterpret_cast<const uint32_t*>(&b);
+}
+
 // RMSNorm of 8 values as HF computes it, bf16(gamma * bf16(x * r)), returned
 // packed as bf16 (the form every later step reads).  Each rounding handles two
-// values per conversion instruction.  Used by the one-row-per-CTA kernels
-// (decode), whose chain of dependent conversions it shortens: the decode step
-// went from 1507 to 1471 us.  The many-row kernels keep one conversion per
-// value: with these helpers they ran slower (68 -> 78 us at 16384 x 2560),
-// although the conversion pipe was 78% busy there.
+// values per conversion instruction.  In the one-row-per-CTA kernels (decode)
+// it shortens the chain of dependent conversions (the decode step went from
+// 1507 to 1471 us); in the many-row kernels it halves the load on the
+// conversion pipe (those need launch bounds of two CTAs per SM: without them
+// the helpers raise the register count past 128 and one CTA fits per SM).
+__device__ __forceinline__ uint32_t aq_norm2(uint32_t x, uint32_t g, uint64_t rr) {
+  const uint32_t y = f2_to_bf2(f2_mul(f2_from_bf2(x), rr));
+  return f2_to_bf2(f2_mul(f2_from_bf2(g), f2_from_bf2(y)));
+}
 __device__ __forceinline__ uint4 aq_norm8(const uint4 xv, const uint4 gv, float r) {
-  float f[8], g[8];
-  aq_unpack8(xv, f);
-  aq_unpack8(gv, g);
-  uint32_t o[4];
-#pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    const __nv_bfloat162 y = __floats2bfloat162_rn(__fmul_rn(f[2 * e], r), __fmul_rn(f[2 * e + 1], r));
-    const uint32_t yb = *reinterpret_cast<const uint32_t*>(&y);
-    const __nv_bfloat162 a = __floats2bfloat162_rn(__fmul_rn(g[2 * e], __uint_as_float(yb << 16)),
-                                                   __fmul_rn(g[2 * e + 1], __uint_as_float(yb & 0xFFFF0000u)));
-    o[e] = *reinterpret_cast<const uint32_t*>(&a);
-  }
-  return make_uint4(o[0], o[1], o[2], o[3]);
+  const uint64_t rr = f2_splat(r);
+  return make_uint4(aq_norm2(xv.x, gv.x, rr), aq_norm2(xv.y, gv.y, rr), aq_norm2(xv.z, gv.z, rr),
+                    aq_norm2(xv.w, gv.w, rr));
 }
 
 // rint(v), half to even, for |v| < 2^22 (the codes: |v| <= 127 plus rounding):
@@ -422,180 +443,162 @@ act_quant_row_kernel(const uint16_t* __restrict__ x, int M, int K, int ldx, cons
   }
 }
 
-// Many-row path (prefill): one warp per token row, 8 rows per CTA, every
-// reduction a warp shuffle (no block barrier).  Lane l keeps chunks
-// l, l + 32, ... (up to MAXC of 8 elements) in registers.  Same results as
+// ---------------------------------------------------------------------------
+// Many-row (prefill) arithmetic on packed bf16 pairs.  These kernels stream
+// 16384 rows per launch and were bound by instruction issue and by the
+// conversion pipe (one f32 -> bf16 conversion per rounding per value, a
+// float -> int conversion per code, clamps and shift-or byte packing).  Per
+// pair of values the helpers below use: shifts to widen bf16 to fp32, one
+// paired conversion per rounding step, a bf16x2 max for the absmax, an add of
+// 1.5 * 2^23 for the half-to-even rounding of the codes, byte permutes for the
+// packing and dp4a for the row sum; the normalisation's fp32 products run as
+// .f32x2 pairs (aq_norm8).  Results are bit-identical to aq_row_vec.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float bf_lo(uint32_t v) { return __uint_as_float(v << 16); }
+__device__ __forceinline__ float bf_hi(uint32_t v) { return __uint_as_float(v & 0xFFFF0000u); }
+
+// x^2 of the two values of a packed pair, each added to its own fp64 chain
+// (squares of bf16 values are exact in fp64).
+__device__ __forceinline__ void aq_sq2(uint32_t v, double& a, double& b) {
+  const double lo = (double)bf_lo(v), hi = (double)bf_hi(v);
+  a = fma(lo, lo, a);
+  b = fma(hi, hi, b);
+}
+__device__ __forceinline__ void aq_sq8(const uint4 v, double (&ss)[4]) {
+  aq_sq2(v.x, ss[0], ss[1]);
+  aq_sq2(v.y, ss[2], ss[3]);
+  aq_sq2(v.z, ss[0], ss[1]);
+  aq_sq2(v.w, ss[2], ss[3]);
+}
+
+// Packed |a| max: the magnitudes of bf16 values are non-negative, and max of
+// two bf16x2 operands is exact.
+__device__ __forceinline__ uint32_t aq_max2(uint32_t a, uint32_t b) {
+  const __nv_bfloat162 r =
+      __hmax2(*reinterpret_cast<const __nv_bfloat162*>(&a), *reinterpret_cast<const __nv_bfloat162*>(&b));
+  return *reinterpret_cast<const uint32_t*>(&r);
+}
+__device__ __forceinline__ uint32_t aq_absmax8(uint32_t m, const uint4 v) {
+  const uint32_t mag = 0x7FFF7FFFu;
+  const uint32_t t0 = aq_max2(v.x & mag, v.y & mag), t1 = aq_max2(v.z & mag, v.w & mag);
+  return aq_max2(m, aq_max2(t0, t1));
+}
+// Row absmax of a warp from each lane's packed max (bits of non-negative bf16
+// values order as the values do).
+__device__ __forceinline__ float aq_warp_absmax(uint32_t m) {
+  const uint32_t b = max(m & 0xFFFFu, m >> 16);
+  return __uint_as_float(__reduce_max_sync(0xffffffffu, b) << 16);
+}
+
+// Codes of four normalised values (two packed pairs): q = rint(a * s) half to
+// even, as the low byte of fp32(a * s) + 1.5 * 2^23 (that sum holds
+// 0x4B400000 + q, whose low byte is q mod 256).  No clamp: |a| <= amax and
+// s = fp32(127 / amax) give |fp32(a * s)| <= 127 (1 + 2^-24)^2 < 127.5, so
+// q lies in [-127, 127] for finite inputs.
+// The product and the add stay scalar: issued as a .f32x2 multiply followed
+// by a .f32x2 add they gave rint of the exact product (33 of 38,400 codes one
+// off at near-ties, measured on B200), not rint(fp32(a * s)).
+__device__ __forceinline__ uint32_t aq_code_bits(float a, float s) {
+  return __float_as_uint(__fadd_rn(__fmul_rn(a, s), 12582912.0f));
+}
+__device__ __forceinline__ uint32_t aq_codes4(uint32_t a01, uint32_t a23, float s) {
+  const uint32_t lo = __byte_perm(aq_code_bits(bf_lo(a01), s), aq_code_bits(bf_hi(a01), s), 0x0040);
+  const uint32_t hi = __byte_perm(aq_code_bits(bf_lo(a23), s), aq_code_bits(bf_hi(a23), s), 0x0040);
+  return __byte_perm(lo, hi, 0x5410);
+}
+
+// Many-row path (prefill, M >= 256, K <= AQ_STAGE_MAX_K): one warp per token
+// row, 8 rows per CTA, every reduction a warp shuffle or redux (no block
+// barrier).  The CTA's 8 rows are staged in shared memory (one bulk copy per
+// row, so a whole row is in flight at once) and read there three times: sum
+// of squares; normalisation (written back in place) and absmax; codes.  HBM
+// reads each row once.  The 8 rows of a CTA share each 128-byte core matrix of
+// the tiled code layout, so the CTA writes whole lines.  Same results as
 // aq_row_vec: fp64 sum of squares (exact in any order), max, integer sum.
-// The 8 rows of a CTA share each 128-byte core matrix of the tiled code
-// layout, so the CTA writes whole lines.  Requirements as for
-// act_quant_vec_kernel, and Kp <= 8 * 32 * MAXC.
-template <int MAXC>
-__global__ void __launch_bounds__(256)
-act_quant_warp_kernel(const uint16_t* __restrict__ x, int M, int K, int ldx, const uint16_t* __restrict__ gamma,
+// Dynamic shared memory: 8 * K * 2 bytes (5 CTAs per SM by shared memory at
+// K = 2560, 2 at K = 6912).  Requirements as for act_quant_vec_kernel.
+constexpr int AQ_STAGE_MAX_K = 14336;  // 8 rows x 2 bytes x K plus the barriers within 227 KB
+__global__ void __launch_bounds__(256, 2)
+act_quant_rows_kernel(const uint16_t* __restrict__ x, int M, int K, int ldx, const uint16_t* __restrict__ gamma,
                       float eps, int8_t* __restrict__ q, float* __restrict__ row_scale, int32_t* __restrict__ row_sum,
                       uint16_t* __restrict__ normed_out, int T, int Kp) {
-  pdl_trigger();
-  const int lane = threadIdx.x & 31;
-  const int m = blockIdx.x * 8 + (threadIdx.x >> 5);
+  extern __shared__ __align__(16) uint8_t aq_stage_smem[];
+  __shared__ uint64_t row_full[8];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int m = blockIdx.x * 8 + warp;
   const bool valid = m < M;
-  const int KC8 = K >> 3;
-  pdl_wait();
-  uint4 xr[MAXC];
-#pragma unroll
-  for (int c = 0; c < MAXC; ++c) {
-    const int ch = lane + 32 * c;
-    xr[c] = (valid && ch < KC8) ? reinterpret_cast<const uint4*>(x + (size_t)m * ldx)[ch] : make_uint4(0, 0, 0, 0);
+  const int KC8 = K >> 3, KP8 = Kp >> 3;
+  uint4* row = reinterpret_cast<uint4*>(aq_stage_smem) + (size_t)warp * KC8;
+  if (lane == 0) {
+    mbar_init(&row_full[warp], 1);
+    fence_mbar_init();
   }
+  __syncwarp();
+  pdl_trigger();
+  pdl_wait();
+  if (valid) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(&row_full[warp], (uint32_t)(K * 2));
+      bulk_g2s(row, x + (size_t)m * ldx, (uint32_t)(K * 2), &row_full[warp]);
+    }
+    // every lane waits, so each one sees the copied row
+    const bool ok = mbar_wait(&row_full[warp], 0, 320);
+    if (!__all_sync(0xffffffffu, ok)) {
+      // a copy that is still in flight must land before the CTA exits
+      if (lane == 0) mbar_wait(&row_full[warp], 0, 321);
+      return;
+    }
+  } else {
+    for (int ch = lane; ch < KC8; ch += 32) row[ch] = make_uint4(0, 0, 0, 0);
+    __syncwarp();
+  }
+  const uint4* grow = reinterpret_cast<const uint4*>(gamma);
+  uint32_t mx = 0;
   if (gamma != nullptr) {
     double ssp[4] = {0.0, 0.0, 0.0, 0.0};  // four independent chains (exact in any order)
-#pragma unroll
-    for (int c = 0; c < MAXC; ++c) {
-      float f[8];
-      aq_unpack8(xr[c], f);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) ssp[e & 3] = fma((double)f[e], (double)f[e], ssp[e & 3]);
-    }
+    // the passes are unrolled so that a lane has several chunks' loads and
+    // conversions in flight (the kernel is bound by their latency)
+#pragma unroll 4
+    for (int ch = lane; ch < KC8; ch += 32) aq_sq8(row[ch], ssp);
     double ss = (ssp[0] + ssp[1]) + (ssp[2] + ssp[3]);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
     const float var = __double2float_rn(__ddiv_rn(ss, (double)K));
     const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
-#pragma unroll
-    for (int c = 0; c < MAXC; ++c) {
-      // gamma is read here, not kept in registers: every row of the launch
-      // reads the same few KB, which stay in L1
-      const int ch = lane + 32 * c;
-      const uint4 gv = ch < KC8 ? reinterpret_cast<const uint4*>(gamma)[ch] : make_uint4(0, 0, 0, 0);
-      float f[8], g[8];
-      aq_unpack8(xr[c], f);
-      aq_unpack8(gv, g);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) f[e] = round_bf16(__fmul_rn(g[e], round_bf16(__fmul_rn(f[e], r))));
-      xr[c] = aq_pack8(f);
-    }
-  }
-  if (normed_out != nullptr && valid) {
-#pragma unroll
-    for (int c = 0; c < MAXC; ++c) {
-      const int ch = lane + 32 * c;
-      if (ch < KC8) reinterpret_cast<uint4*>(normed_out + (size_t)m * K)[ch] = xr[c];
-    }
-  }
-  if (q == nullptr) return;
-  float amax = 0.f;
-#pragma unroll
-  for (int c = 0; c < MAXC; ++c) {
-    float f[8];
-    aq_unpack8(xr[c], f);
-#pragma unroll
-    for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(f[e]));
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-  amax = fmaxf(amax, 1e-5f);
-  const float s = __fdiv_rn(127.0f, amax);
-  int qsum = 0;
-#pragma unroll
-  for (int c = 0; c < MAXC; ++c) {
-    const int ch = lane + 32 * c;
-    if (ch * 8 < Kp) {  // chunks past K (up to Kp) are written as zeros
-      float f[8];
-      aq_unpack8(xr[c], f);
-      uint32_t lo = 0, hi = 0;
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        int qi = 0;
-        if (valid && ch < KC8) qi = max(-128, min(127, __float2int_rn(__fmul_rn(f[e], s))));
-        qsum += qi;
-        if (e < 4)
-          lo |= ((uint32_t)(qi & 0xFF)) << (8 * e);
-        else
-          hi |= ((uint32_t)(qi & 0xFF)) << (8 * (e - 4));
-      }
-      *reinterpret_cast<uint2*>(q + alayout_offset(m, ch * 8, T, Kp)) = make_uint2(lo, hi);
-    }
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) qsum += __shfl_xor_sync(0xffffffffu, qsum, o);
-  if (lane == 0) {
-    row_scale[m] = valid ? s : 1.0f;
-    row_sum[m] = qsum;
-  }
-}
-
-// Many-row path for long rows (K > 2560, the FFN width): one warp per row as
-// above, but the row is not held in registers; it is read three times (sum of
-// squares, absmax of the normalised values, codes).  A CTA's 8 rows (at most
-// 8 x 16 KB) stay in L1 between the passes, so DRAM reads the row once.
-__global__ void __launch_bounds__(256)
-act_quant_warp_stream_kernel(const uint16_t* __restrict__ x, int M, int K, int ldx, const uint16_t* __restrict__ gamma,
-                             float eps, int8_t* __restrict__ q, float* __restrict__ row_scale,
-                             int32_t* __restrict__ row_sum, uint16_t* __restrict__ normed_out, int T, int Kp) {
-  pdl_trigger();
-  pdl_wait();
-  const int lane = threadIdx.x & 31;
-  const int m = blockIdx.x * 8 + (threadIdx.x >> 5);
-  const bool valid = m < M;
-  const int KC8 = K >> 3, KP8 = Kp >> 3;
-  const uint4* xrow = reinterpret_cast<const uint4*>(x + (size_t)m * ldx);
-  const uint4* grow = reinterpret_cast<const uint4*>(gamma);
-  float r = 1.f;
-  if (gamma != nullptr) {
-    double ssp[4] = {0.0, 0.0, 0.0, 0.0};  // four independent chains (exact in any order)
+#pragma unroll 4
     for (int ch = lane; ch < KC8; ch += 32) {
-      float f[8];
-      aq_unpack8(valid ? xrow[ch] : make_uint4(0, 0, 0, 0), f);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) ssp[e & 3] = fma((double)f[e], (double)f[e], ssp[e & 3]);
+      const uint4 a = aq_norm8(row[ch], grow[ch], r);
+      row[ch] = a;
+      if (normed_out != nullptr && valid) reinterpret_cast<uint4*>(normed_out + (size_t)m * K)[ch] = a;
+      mx = aq_absmax8(mx, a);
     }
-    double ss = (ssp[0] + ssp[1]) + (ssp[2] + ssp[3]);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    const float var = __double2float_rn(__ddiv_rn(ss, (double)K));
-    r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
-  }
-  // normalised chunk ch (packed bf16) -> f
-  auto chunk = [&](int ch, float* f) {
-    aq_unpack8((valid && ch < KC8) ? xrow[ch] : make_uint4(0, 0, 0, 0), f);
-    if (gamma != nullptr) {
-      float g[8];
-      aq_unpack8(ch < KC8 ? grow[ch] : make_uint4(0, 0, 0, 0), g);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) f[e] = round_bf16(__fmul_rn(g[e], round_bf16(__fmul_rn(f[e], r))));
+  } else {
+    for (int ch = lane; ch < KC8; ch += 32) {
+      if (normed_out != nullptr && valid) reinterpret_cast<uint4*>(normed_out + (size_t)m * K)[ch] = row[ch];
+      mx = aq_absmax8(mx, row[ch]);
     }
-  };
-  float amax = 0.f;
-  for (int ch = lane; ch < KC8; ch += 32) {
-    float f[8];
-    chunk(ch, f);
-    if (normed_out != nullptr && valid) reinterpret_cast<uint4*>(normed_out + (size_t)m * K)[ch] = aq_pack8(f);
-#pragma unroll
-    for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(f[e]));
   }
   if (q == nullptr) return;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-  amax = fmaxf(amax, 1e-5f);
+  const float amax = fmaxf(aq_warp_absmax(mx), 1e-5f);
   const float s = __fdiv_rn(127.0f, amax);
   int qsum = 0;
-  for (int ch = lane; ch < KP8; ch += 32) {  // chunks past K (up to Kp) are written as zeros
-    float f[8];
-    chunk(ch, f);
-    uint32_t lo = 0, hi = 0;
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      int qi = 0;
-      if (valid && ch < KC8) qi = max(-128, min(127, __float2int_rn(__fmul_rn(f[e], s))));
-      qsum += qi;
-      if (e < 4)
-        lo |= ((uint32_t)(qi & 0xFF)) << (8 * e);
-      else
-        hi |= ((uint32_t)(qi & 0xFF)) << (8 * (e - 4));
+  // chunk ch of the row sits at alayout_offset(m, 8 ch); 32 chunks further on
+  // (256 codes) it is 16 core-matrix columns = 256 T bytes further on
+  int8_t* qp = q + alayout_offset(m, lane * 8, T, Kp);
+  const size_t qstep = (size_t)256 * T;
+#pragma unroll 4
+  for (int ch = lane; ch < KP8; ch += 32, qp += qstep) {  // chunks past K (up to Kp) are written as zeros
+    uint2 o = make_uint2(0, 0);
+    if (valid && ch < KC8) {
+      const uint4 a = row[ch];
+      o.x = aq_codes4(a.x, a.y, s);
+      o.y = aq_codes4(a.z, a.w, s);
     }
-    *reinterpret_cast<uint2*>(q + alayout_offset(m, ch * 8, T, Kp)) = make_uint2(lo, hi);
+    qsum = __dp4a((int)o.x, 0x01010101, qsum);
+    qsum = __dp4a((int)o.y, 0x01010101, qsum);
+    *reinterpret_cast<uint2*>(qp) = o;
   }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) qsum += __shfl_xor_sync(0xffffffffu, qsum, o);
+  qsum = __reduce_add_sync(0xffffffffu, qsum);
   if (lane == 0) {
     row_scale[m] = valid ? s : 1.0f;
     row_sum[m] = qsum;

@@ -174,7 +174,7 @@ int to_dev_segments(const bitnet_segments_t* s, int N, int epilogue, bitnet_segm
   return s->end[s->count - 1] == N ? BITNET_OK : BITNET_ERR_INVALID_ARGUMENT;
 }
 
-std::atomic<unsigned long long> g_smem_aq{0}, g_smem_simt[3][4], g_smem_tc[3], g_smem_lmh{0}, g_smem_att[4],
+std::atomic<unsigned long long> g_smem_aq{0}, g_smem_aq_stage{0}, g_smem_simt[3][4], g_smem_tc[3], g_smem_lmh{0}, g_smem_att[4],
     g_smem_apf{0};
 
 int lm_head_tile_T(int B) { return round_up(B, 16); }
@@ -437,11 +437,13 @@ int bitnet_act_quant(const void* x, int M, int K, int ldx, const void* gamma, fl
   const int rows = want_q ? act_rows_of(M) : M;
   const bool vec_ok = K % 8 == 0 && ldx % 8 == 0 && aligned(x, 16) && (!gamma || aligned(gamma, 16)) &&
                       (!normed_out || aligned(normed_out, 16));
-  // many rows: a warp per row (the rows are padded to whole token tiles, multiples of 8)
-  if (vec_ok && M >= 256 && rows % 8 == 0) {
-    auto k = Kp <= 8 * 32 * 10 ? act_quant_warp_kernel<10> : act_quant_warp_stream_kernel;
-    return launch(k, dim3(rows / 8), dim3(256), 0, stream, 1, (const uint16_t*)x, M, K, ldx, (const uint16_t*)gamma,
-                  eps, q, row_scale, row_sum, (uint16_t*)normed_out, act_tile_of(M), Kp);
+  // many rows: a warp per row, rows staged in shared memory (the rows are padded to whole token tiles,
+  // multiples of 8)
+  if (vec_ok && M >= 256 && rows % 8 == 0 && K <= AQ_STAGE_MAX_K) {
+    if (int e = ensure_smem(act_quant_rows_kernel, &g_smem_aq_stage)) return e;
+    return launch(act_quant_rows_kernel, dim3(rows / 8), dim3(256), (size_t)16 * K, stream, 1,
+                  (const uint16_t*)x, M, K, ldx, (const uint16_t*)gamma, eps, q, row_scale, row_sum,
+                  (uint16_t*)normed_out, act_tile_of(M), Kp);
   }
   // few rows: one CTA per row, one thread per chunk of 8 (two or four chunks
   // per thread for rows longer than 8192)

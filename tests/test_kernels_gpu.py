@@ -109,7 +109,9 @@ def run_act_quant(x: torch.Tensor, gamma: torch.Tensor | None, eps: float, cuda)
 @pytest.mark.parametrize("m,k", [(1, 64), (3, 100), (8, 2560), (32, 2560), (32, 6912), (40, 320), (300, 128),
                                  (2, 8192), (2, 8200),
                                  # many rows: one warp per row (prefill), both register budgets, ragged last tile
-                                 (260, 2560), (520, 6912), (1024, 7168), (256, 8192)])
+                                 (260, 2560), (520, 6912), (1024, 7168), (256, 8192),
+                                 # the longest rows staged in shared memory, and the first that are not
+                                 (264, 14336), (256, 14400)])
 @pytest.mark.parametrize("with_gamma", [True, False])
 def test_act_quant_bit_exact(cuda, m, k, with_gamma):
     x = rand_bf16((m, k), seed=m * 1000 + k)
@@ -122,7 +124,8 @@ def test_act_quant_bit_exact(cuda, m, k, with_gamma):
     np.testing.assert_array_equal(rsum, ref["row_sum"])
 
 
-def test_act_quant_edge_rows(cuda):
+@pytest.mark.parametrize("reps", [1, 52])  # 5 rows (one CTA per row), 260 rows (one warp per row, prefill)
+def test_act_quant_edge_rows(cuda, reps):
     k = 96
     x = np.zeros((5, k), np.float32)
     x[1, :] = 1e4 * np.linspace(-1, 1, k)        # large values
@@ -130,14 +133,15 @@ def test_act_quant_edge_rows(cuda):
     x[2, 1:8] = [0.5, 1.5, 2.5, -0.5, -1.5, -2.5, 3.5]  # exact .5 ties
     x[3, :] = 1e-30                               # below the 1e-5 absmax clamp
     x[4, :] = np.linspace(-3, 3, k)
-    xt = torch.from_numpy(x).to(torch.bfloat16)
+    xt = torch.from_numpy(np.tile(x, (reps, 1))).to(torch.bfloat16)
     q, s, rsum, _ = run_act_quant(xt, None, 1e-5, cuda)
     ref = ob.bitlinear(f32(xt), None, 1e-5, np.zeros((1, k), np.int8))
     np.testing.assert_array_equal(q, ref["q"])
     np.testing.assert_array_equal(s, ref["s"])
     np.testing.assert_array_equal(rsum, ref["row_sum"])
-    assert s[2] == 1.0 and q[2, :8].tolist() == [127, 0, 2, 2, 0, -2, -2, 4]
-    assert not q[0].any() and not q[3].any()
+    for j in range(0, 5 * reps, 5):
+        assert s[j + 2] == 1.0 and q[j + 2, :8].tolist() == [127, 0, 2, 2, 0, -2, -2, 4]
+        assert not q[j].any() and not q[j + 3].any()
 
 
 # ---------------------------------------------------------------------------
@@ -307,7 +311,8 @@ def test_bounded_wait_gives_up_with_a_status_and_the_context_stays_usable(cuda):
 
 @pytest.mark.filterwarnings("ignore:overflow encountered")
 @pytest.mark.parametrize("k", [2560, 6912])
-def test_act_quant_extreme_dynamic_range_rows(cuda, k):
+@pytest.mark.parametrize("reps", [1, 33])  # 8 rows (one CTA per row), 264 rows (one warp per row, prefill)
+def test_act_quant_extreme_dynamic_range_rows(cuda, k, reps):
     """Rows at the edges of the bf16 range (1e-20 mixed with 1e17, magnitudes over
     2^-30 .. 2^30, an overflowing variance, subnormals only, ...): the kernel's
     codes, scales, row sums and normalised values equal the oracle's wherever the
@@ -317,7 +322,7 @@ def test_act_quant_extreme_dynamic_range_rows(cuda, k):
 
     rows = extreme_rows(k, seed=k)
     gamma = (1 + 0.1 * rand_bf16((k,), seed=k + 1).float()).to(torch.bfloat16)
-    x = torch.from_numpy(rows).to(torch.bfloat16)
+    x = torch.from_numpy(np.tile(rows, (reps, 1))).to(torch.bfloat16)
     q, s, rsum, normed = run_act_quant(x, gamma, 1e-5, cuda)
     ref = ob.bitlinear(rows, f32(gamma), 1e-5, np.zeros((1, k), np.int8))
     order_dependent = []
@@ -325,7 +330,8 @@ def test_act_quant_extreme_dynamic_range_rows(cuda, k):
         if len(set(var_orders(rows[i]).values())) != 1:
             order_dependent.append(name)
             continue
-        np.testing.assert_array_equal(normed[i], ref["normed"][i], err_msg=name)
-        np.testing.assert_array_equal(q[i], ref["q"][i], err_msg=name)
-        assert s[i] == ref["s"][i] and rsum[i] == ref["row_sum"][i], name
+        for j in range(i, len(ROW_NAMES) * reps, len(ROW_NAMES)):
+            np.testing.assert_array_equal(normed[j], ref["normed"][i], err_msg=name)
+            np.testing.assert_array_equal(q[j], ref["q"][i], err_msg=name)
+            assert s[j] == ref["s"][i] and rsum[j] == ref["row_sum"][i], name
     assert not order_dependent, f"rows whose fp32 variance depends on the summation order: {order_dependent}"
