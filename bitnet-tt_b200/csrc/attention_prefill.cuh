@@ -6,7 +6,9 @@
 //     out[i]    = bf16(bf16(x[i] * cos_i)    + bf16(-x[i+64] * sin_i))
 //     out[i+64] = bf16(bf16(x[i+64] * cos_i) + bf16( x[i]    * sin_i))
 // Rotated queries go to q_out [B*P, n_heads*128]; rotated keys and the values
-// go to the caches at rows p = 0 .. P-1.
+// go to the caches at rows p = 0 .. P-1.  rope_append_prefill_vec_kernel does
+// the same with 16-byte accesses, .f32x2 arithmetic and 8 tokens per CTA when
+// every pointer is 16-byte aligned.
 //
 // attention_prefill_kernel: CTA = (query block of 64 tokens, query head, sequence),
 // 4 warps of 16 query rows.  Key blocks of 64 up to the diagonal: K and V rows
@@ -95,6 +97,88 @@ __global__ void __launch_bounds__(256) rope_append_prefill_kernel(const RopePref
       const uint16_t* vsrc = row + (size_t)(p.n_heads + p.n_kv + g) * ATT_D;
       *reinterpret_cast<uint32_t*>(p.v_cache + crow + d) = *reinterpret_cast<const uint32_t*>(vsrc + d);
       *reinterpret_cast<uint32_t*>(p.v_cache + crow + 64 + d) = *reinterpret_cast<const uint32_t*>(vsrc + 64 + d);
+    }
+  }
+}
+
+// The same rotation for two dims of each half (packed bf16 pairs x1 = dims
+// (d, d+1), x2 = dims (d+64, d+65)): every product and sum as an .f32x2 pair,
+// every rounding one paired conversion.  -x2 * sin is (-x2) * sin with the sign
+// flipped on the bf16 bits, as the scalar form computes it.  The adds only see
+// bf16-rounded operands.
+__device__ __forceinline__ void rope_rotate2(uint32_t x1, uint32_t x2, uint32_t c, uint32_t s, uint32_t& o1,
+                                             uint32_t& o2) {
+  const uint64_t a = f2_from_bf2(x1), b = f2_from_bf2(x2), nb = f2_from_bf2(x2 ^ 0x80008000u);
+  const uint64_t cc = f2_from_bf2(c), ss = f2_from_bf2(s);
+  o1 = f2_to_bf2(f2_add(f2_from_bf2(f2_to_bf2(f2_mul(a, cc))), f2_from_bf2(f2_to_bf2(f2_mul(nb, ss)))));
+  o2 = f2_to_bf2(f2_add(f2_from_bf2(f2_to_bf2(f2_mul(b, cc))), f2_from_bf2(f2_to_bf2(f2_mul(a, ss)))));
+}
+
+// 16-byte form of rope_append_prefill_kernel (every pointer 16-byte aligned):
+// a CTA takes RPF_TOK tokens; a work item is 8 dims of both halves of one
+// rotated head (query or key; 8 items a head) or 8 dims of one value head (16
+// items a head), so each access moves 16 bytes.  Bit-identical results.
+constexpr int RPF_TOK = 8;
+__global__ void __launch_bounds__(256) rope_append_prefill_vec_kernel(const RopePrefillParams p, int tokens) {
+  __shared__ int s_b[RPF_TOK], s_pos[RPF_TOK];
+  pdl_trigger();
+  pdl_wait();
+  const int tok0 = blockIdx.x * RPF_TOK;
+  if (threadIdx.x < RPF_TOK) {
+    const int tok = tok0 + threadIdx.x;
+    int b = -1, pos = 0;
+    if (tok < tokens) {
+      if (p.cu != nullptr) {
+        int lo = 0, hi = p.B;
+        while (hi - lo > 1) {
+          const int mid = (lo + hi) >> 1;
+          if (p.cu[mid] <= tok) lo = mid; else hi = mid;
+        }
+        pos = tok - p.cu[lo];
+        if (pos < 0 || tok >= p.cu[lo + 1] || pos >= p.max_len || pos >= p.rope_len)
+          record_error(DEV_ERR_BOUNDS, 330);
+        else
+          b = lo;
+      } else {
+        pos = tok % p.P;
+        b = tok / p.P;
+      }
+    }
+    s_b[threadIdx.x] = b;
+    s_pos[threadIdx.x] = pos;
+  }
+  __syncthreads();
+  const int rot_items = (p.n_heads + p.n_kv) * 8, per_tok = rot_items + p.n_kv * 16;
+  const size_t row_elems = (size_t)(p.n_heads + 2 * p.n_kv) * ATT_D;
+  for (int it = threadIdx.x; it < RPF_TOK * per_tok; it += blockDim.x) {
+    const int t = it / per_tok, r = it - t * per_tok;
+    const int b = s_b[t];
+    if (b < 0) continue;
+    const int tok = tok0 + t, pos = s_pos[t];
+    const uint16_t* row = p.qkv + (size_t)tok * row_elems;
+    if (r < rot_items) {
+      const int hh = r >> 3, d = (r & 7) * 8;
+      const uint4 x1 = *reinterpret_cast<const uint4*>(row + hh * ATT_D + d);
+      const uint4 x2 = *reinterpret_cast<const uint4*>(row + hh * ATT_D + 64 + d);
+      const uint4 c = *reinterpret_cast<const uint4*>(p.rope_cos + (size_t)pos * 64 + d);
+      const uint4 s = *reinterpret_cast<const uint4*>(p.rope_sin + (size_t)pos * 64 + d);
+      uint4 o1, o2;
+      rope_rotate2(x1.x, x2.x, c.x, s.x, o1.x, o2.x);
+      rope_rotate2(x1.y, x2.y, c.y, s.y, o1.y, o2.y);
+      rope_rotate2(x1.z, x2.z, c.z, s.z, o1.z, o2.z);
+      rope_rotate2(x1.w, x2.w, c.w, s.w, o1.w, o2.w);
+      uint16_t* dst;
+      if (hh < p.n_heads)
+        dst = p.q_out + (size_t)tok * (size_t)(p.n_heads * ATT_D) + hh * ATT_D;
+      else
+        dst = p.k_cache + (((size_t)b * p.n_kv + (hh - p.n_heads)) * p.max_len + pos) * ATT_D;
+      *reinterpret_cast<uint4*>(dst + d) = o1;
+      *reinterpret_cast<uint4*>(dst + 64 + d) = o2;
+    } else {
+      const int v = r - rot_items, g = v >> 4, c8 = (v & 15) * 8;
+      const size_t crow = (((size_t)b * p.n_kv + g) * p.max_len + pos) * ATT_D;
+      *reinterpret_cast<uint4*>(p.v_cache + crow + c8) =
+          *reinterpret_cast<const uint4*>(row + (size_t)(p.n_heads + p.n_kv + g) * ATT_D + c8);
     }
   }
 }

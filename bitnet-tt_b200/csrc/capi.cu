@@ -644,6 +644,11 @@ static int rope_prefill_impl(const void* qkv, int B, int P, const int32_t* cu, i
   p.k_cache = (uint16_t*)k_cache;
   p.v_cache = (uint16_t*)v_cache;
   p.max_len = max_len;
+  // 16-byte accesses when every pointer allows them (the row strides are multiples of 256 bytes)
+  if (aligned(qkv, 16) && aligned(q_out, 16) && aligned(k_cache, 16) && aligned(v_cache, 16) &&
+      aligned(rope_cos, 16) && aligned(rope_sin, 16))
+    return launch(rope_append_prefill_vec_kernel, dim3((tokens + RPF_TOK - 1) / RPF_TOK), dim3(256), 0, stream, 1,
+                  p, tokens);
   return launch(rope_append_prefill_kernel, dim3(tokens), dim3(256), 0, stream, 1, p);
 }
 

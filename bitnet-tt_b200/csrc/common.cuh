@@ -347,4 +347,40 @@ __host__ __device__ __forceinline__ size_t alayout_offset(int m, int k, int T, i
          (size_t)(k & 15);
 }
 
+// ---------------------------------------------------------------------------
+// Pairs of fp32 values in one 64-bit register, for the sm_100 .f32x2
+// arithmetic: one instruction performs two IEEE round-to-nearest operations,
+// each exactly as its scalar form.  Element 0 sits in the low half.
+__device__ __forceinline__ uint64_t f2_make(uint32_t lo_bits, uint32_t hi_bits) {
+  uint64_t d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "r"(lo_bits), "r"(hi_bits));
+  return d;
+}
+__device__ __forceinline__ void f2_split(uint64_t a, uint32_t& lo_bits, uint32_t& hi_bits) {
+  asm("mov.b64 {%0, %1}, %2;" : "=r"(lo_bits), "=r"(hi_bits) : "l"(a));
+}
+__device__ __forceinline__ uint64_t f2_splat(float v) { return f2_make(__float_as_uint(v), __float_as_uint(v)); }
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+// Do not feed an f2_mul result straight into f2_add: on B200 that pair gave
+// the rounding of the exact sum (as a fused multiply-add would), not two
+// roundings.  Add only operands that went through another rounding step.
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+// two packed bf16 values -> an fp32 pair (exact: a bf16 is the top half of an fp32)
+__device__ __forceinline__ uint64_t f2_from_bf2(uint32_t v) { return f2_make(v << 16, v & 0xFFFF0000u); }
+// fp32 pair -> two bf16 values, each rounded to nearest even, one conversion
+__device__ __forceinline__ uint32_t f2_to_bf2(uint64_t a) {
+  uint32_t lo, hi;
+  f2_split(a, lo, hi);
+  const __nv_bfloat162 b = __floats2bfloat162_rn(__uint_as_float(lo), __uint_as_float(hi));
+  return *reinterpret_cast<const uint32_t*>(&b);
+}
+
 }  // namespace bitnet

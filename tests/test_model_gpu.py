@@ -171,6 +171,45 @@ def _prefill_attention_case(cuda, b, plen, nh, nkv, max_len, seed=5):
     np.testing.assert_allclose(out.float().cpu().numpy(), ref.numpy(), rtol=2e-2, atol=2e-2)
 
 
+@pytest.mark.parametrize("ragged", [False, True])
+def test_rope_append_prefill_4byte_aligned_buffers_match(cuda, ragged):
+    """Buffers that are 4- but not 16-byte aligned take the 4-byte kernel; 16-byte
+    aligned ones the 16-byte kernel.  Both write identical queries and cache rows."""
+    from bitnet_tt import _lib
+    from bitnet_tt.utils.rope import half_split_tables
+
+    b, plen, nh, nkv, max_len, d = 3, 37, 4, 2, 48, 128
+    g = torch.Generator().manual_seed(21)
+    qkv = torch.randn((b * plen, (nh + 2 * nkv) * d), generator=g).to(torch.bfloat16)
+    cos, sin = half_split_tables(d, max_len, 500000.0)
+
+    def offset_copy(t, off):  # same values at a data pointer 2 * off bytes past a 256-byte aligned base
+        buf = torch.zeros(t.numel() + off, dtype=t.dtype, device=cuda)
+        v = buf[off:].view(t.shape)
+        v.copy_(t.to(cuda))
+        return v
+
+    results = []
+    for off in (0, 2):
+        args = [offset_copy(x, off) for x in (qkv, cos, sin)]
+        q = offset_copy(torch.zeros((b * plen, nh * d), dtype=torch.bfloat16), off)
+        kd = offset_copy(torch.zeros((b, nkv, max_len, d), dtype=torch.bfloat16), off)
+        vd = offset_copy(torch.zeros((b, nkv, max_len, d), dtype=torch.bfloat16), off)
+        assert (q.data_ptr() % 16 == 0) == (off == 0) and q.data_ptr() % 4 == 0
+        if ragged:
+            lens = [37, 5, 20]
+            x = args[0][: sum(lens)]
+            cu = torch.tensor([0, 37, 42, 62], dtype=torch.int32, device=cuda)
+            _lib.rope_append_prefill_varlen(x, cu, max(lens), nh, nkv, args[1], args[2], q[: sum(lens)], kd, vd)
+        else:
+            _lib.rope_append_prefill(args[0], b, plen, nh, nkv, args[1], args[2], q, kd, vd)
+        torch.cuda.synchronize()
+        assert _lib.last_device_status()[0] == 0
+        results.append((q.cpu(), kd.cpu(), vd.cpu()))
+    for a, c in zip(*results):
+        assert torch.equal(a, c)
+
+
 @pytest.mark.parametrize("b,plen,nh,nkv,max_len", [
     (2, 150, 4, 2, 160),    # ragged last query / key block
     (1, 64, 8, 1, 64),      # group of 8 query heads, cache exactly the prompt
