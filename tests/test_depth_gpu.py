@@ -193,7 +193,17 @@ def _teacher_forced_prefill_and_steps(name, gen, oracle, prompts, steps, cap):
 def _free_running(name, gen, oracle, prompts, steps, cap):
     """Both sides on their own states from the same prompts (device: prefill +
     graph replays); the device's distance to the oracle against the distance
-    of the float64-attention oracle to the float32 one (the noise floor)."""
+    of the float64-attention oracle to the float32 one (the noise floor).
+
+    A sequence is compared while its greedy ids agree with the oracle's: once
+    they differ, its next position has another input token, so its logits are
+    no longer comparable (random-init weights put many rows on near-ties, and
+    the float64 oracle itself leaves the float32 trajectory within a few
+    steps).  A flip is a consequence of the logits error, since each side takes
+    the argmax of its own row, so the bound is on that error: over the rows still in
+    step, the device's relative logits error at each position stays below
+    max(2e-2, 3 x the floor's over its own rows in step, or its last value
+    once none is)."""
     b = prompts.shape[0]
     floor_oracle = om.OracleBitNet.__new__(om.OracleBitNet)
     floor_oracle.__dict__.update(oracle.__dict__)  # same weights; attention summed in float64
@@ -216,15 +226,26 @@ def _free_running(name, gen, oracle, prompts, steps, cap):
         gen.step()  # graph replay on the device's own ids
         dev.append((gen.state.ids.cpu().clone(), gen.state.logits.float().cpu().clone()))
     ref, flo = runs
-    dev_rel = [_rel(d[1], r[1]) for d, r in zip(dev, ref)]
-    floor_rel = [_rel(f[1], r[1]) for f, r in zip(flo, ref)]
-    dev_ids = sum(int((d[0].long() != r[0].long()).sum()) for d, r in zip(dev, ref))
-    floor_ids = sum(int((f[0].long() != r[0].long()).sum()) for f, r in zip(flo, ref))
+    in_step = {"device": torch.ones(b, dtype=torch.bool), "floor": torch.ones(b, dtype=torch.bool)}
+    rels = {"device": [], "floor": []}
+    flips = {"device": [], "floor": []}
+    for t in range(steps + 1):
+        r_ids, r_log = ref[t]
+        for side, (ids, log) in (("device", dev[t]), ("floor", flo[t])):
+            live = in_step[side]
+            rels[side].append(_rel(log[live], r_log[live]) if bool(live.any()) else None)
+            diff = (ids.long() != r_ids.long()) & live
+            flips[side] += [(t, s) for s in diff.nonzero().flatten().tolist()]
+            in_step[side] = live & ~diff
+    fmt = lambda xs: ["-" if x is None else "%.2e" % x for x in xs]  # noqa: E731
     _report(f"{name} free-running ({steps + 1} positions x {b} sequences): device vs oracle logits rel err "
-            f"{['%.2e' % x for x in dev_rel]}, {dev_ids} ids differ; float64- vs float32-attention oracle "
-            f"{['%.2e' % x for x in floor_rel]}, {floor_ids} ids differ")
-    for t, (d, f) in enumerate(zip(dev_rel, floor_rel)):
-        assert d < max(2e-2, 3 * f), f"{name} free-running position {t}: device {d:.3e} vs floor {f:.3e}"
+            f"{fmt(rels['device'])} over the sequences still in step, first id flips (position, sequence) "
+            f"{flips['device']}; float64- vs float32-attention oracle {fmt(rels['floor'])}, flips {flips['floor']}")
+    f_seen = 0.0  # a floor whose rows all left the oracle's ids keeps its last measured value
+    for t, (d, f) in enumerate(zip(rels["device"], rels["floor"])):
+        f_seen = f if f is not None else f_seen
+        if d is not None:
+            assert d < max(2e-2, 3 * f_seen), f"{name} free-running position {t}: device {d:.3e} vs floor {f_seen:.3e}"
 
 
 def test_config2_batch32_prefill_and_decode(full_model):
