@@ -360,6 +360,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2) bitlinear_tc_kernel(const TcPar
   const int row_lo = nb * 128, row_hi = min(N, row_lo + 128) - 1;
   const bool seg_uniform = (EPI == EPI_RELU2_MUL) || seg_scale_of(p.seg, row_lo) == seg_scale_of(p.seg, row_hi);
   const int used_acc = min(NACC, 2 * (kc_end - kc_begin));
+  const bool small_acc = KC <= 256;  // K <= 16384: |acc| < 2^22, float(acc) by i2f_exact
 
   if (split == 1) {
     // Whole-K tile: no exchange.  Phase 1: the unpacker warps read D (thread =
@@ -402,12 +403,21 @@ __global__ void __launch_bounds__(TC_THREADS, 2) bitlinear_tc_kernel(const TcPar
           const float4 f4 = *reinterpret_cast<const float4*>(&fac[c + 4 * j4]);
           const int rsv[4] = {rs.x, rs.y, rs.z, rs.w};
           const float fv[4] = {f4.x, f4.y, f4.z, f4.w};
+          float v[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const int j = 4 * j4 + e, m = c + j;
             acc[j] = (int)sum[j] - rsv[e];
-            const float v = fast ? round_bf16(__fmul_rn((float)acc[j], fv[e])) : scaled_bf16(acc[j], wsc, ctrl->scale[m]);
-            st[m * TC_ST_LD + col] = f32_to_bf16_bits(v);
+            v[e] = fast ? __fmul_rn(i2f_exact(acc[j], small_acc), fv[e]) : scaled_bf16(acc[j], wsc, ctrl->scale[m]);
+          }
+          // bf16 of two tokens per conversion (rounding a bf16 value again changes nothing)
+#pragma unroll
+          for (int e = 0; e < 4; e += 2) {
+            const int m = c + 4 * j4 + e;
+            const __nv_bfloat162 b2 = __floats2bfloat162_rn(v[e], v[e + 1]);
+            const uint32_t bits = *reinterpret_cast<const uint32_t*>(&b2);
+            st[m * TC_ST_LD + col] = (uint16_t)(bits & 0xFFFFu);
+            st[(m + 1) * TC_ST_LD + col] = (uint16_t)(bits >> 16);
           }
         }
         if (p.acc_out != nullptr && n < N) {
@@ -458,25 +468,23 @@ __global__ void __launch_bounds__(TC_THREADS, 2) bitlinear_tc_kernel(const TcPar
           if (c0 >= ncols) continue;
           const size_t o = (size_t)(mt * T + m) * Nout + col0 + c0;
           const uint16_t* sv = st + m * TC_ST_LD + c0;
-          alignas(16) uint16_t out[8];
+          uint4 o4;
           if (EPI == EPI_RELU2_MUL) {
             const uint4 g4 = *reinterpret_cast<const uint4*>(sv);
             const uint4 u4 = *reinterpret_cast<const uint4*>(sv + 64);
-            const uint16_t* g = reinterpret_cast<const uint16_t*>(&g4);
-            const uint16_t* uu = reinterpret_cast<const uint16_t*>(&u4);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) out[e] = relu2_mul_bf16(bf16_bits_to_f32(g[e]), bf16_bits_to_f32(uu[e]));
+            o4 = make_uint4(relu2_mul_bf2(g4.x, u4.x), relu2_mul_bf2(g4.y, u4.y), relu2_mul_bf2(g4.z, u4.z),
+                            relu2_mul_bf2(g4.w, u4.w));
           } else {
             const uint4 v4 = *reinterpret_cast<const uint4*>(sv);
-            const uint16_t* v = reinterpret_cast<const uint16_t*>(&v4);
-            const uint16_t* rs = reinterpret_cast<const uint16_t*>(&res[u]);
-#pragma unroll
-            for (int e = 0; e < 8; ++e)
-              out[e] = (EPI == EPI_RESIDUAL_ADD) ? residual_add_bf16(rs[e], bf16_bits_to_f32(v[e])) : v[e];
+            o4 = (EPI == EPI_RESIDUAL_ADD)
+                     ? make_uint4(residual_add_bf2(res[u].x, v4.x), residual_add_bf2(res[u].y, v4.y),
+                                  residual_add_bf2(res[u].z, v4.z), residual_add_bf2(res[u].w, v4.w))
+                     : v4;
           }
           if (vec && c0 + 8 <= ncols) {
-            *reinterpret_cast<uint4*>(p.y + o) = *reinterpret_cast<const uint4*>(out);
+            *reinterpret_cast<uint4*>(p.y + o) = o4;
           } else {
+            const uint16_t* out = reinterpret_cast<const uint16_t*>(&o4);
             for (int e = 0; e < 8 && c0 + e < ncols; ++e) p.y[o + e] = out[e];
           }
         }
@@ -574,8 +582,8 @@ __global__ void __launch_bounds__(TC_THREADS, 2) bitlinear_tc_kernel(const TcPar
           ag += rg[j * slot_ints + m * 128];
           au += ru[j * slot_ints + m * 128];
         }
-        const float g = round_bf16(__fmul_rn((float)ag, ctrl->fac0[m]));
-        const float u = round_bf16(__fmul_rn((float)au, ctrl->fac1[m]));
+        const float g = round_bf16(__fmul_rn(i2f_exact(ag, small_acc), ctrl->fac0[m]));
+        const float u = round_bf16(__fmul_rn(i2f_exact(au, small_acc), ctrl->fac1[m]));
         const uint16_t h = relu2_mul_bf16(g, u);
         if (row_ok && mg < p.M) {
           yb[(size_t)mg * (N >> 1)] = h;
@@ -613,7 +621,8 @@ __global__ void __launch_bounds__(TC_THREADS, 2) bitlinear_tc_kernel(const TcPar
           const int mg = mt * T + m;
           int a = -ctrl->rsum[m];
           for (int j = 0; j < split; ++j) a += rr[j * slot_ints + m * 128];
-          const float v = seg_uniform ? round_bf16(__fmul_rn((float)a, ctrl->fac0[m])) : scaled_bf16(a, wsc, ctrl->scale[m]);
+          const float v = seg_uniform ? round_bf16(__fmul_rn(i2f_exact(a, small_acc), ctrl->fac0[m]))
+                                      : scaled_bf16(a, wsc, ctrl->scale[m]);
           if (row_ok && mg < p.M) {
             const size_t o = (size_t)mg * N + n;
             if (p.acc_out) p.acc_out[o] = a;

@@ -27,6 +27,13 @@ __device__ __forceinline__ float seg_scale_of(const bitnet_segments_dev& seg, in
   return s;
 }
 
+// float(acc) without the conversion pipe when |acc| < 2^22 (small): the bits
+// of 1.5 * 2^23 plus acc are the float 1.5 * 2^23 + acc, and subtracting
+// 1.5 * 2^23 is exact.  |acc| <= 127 K, so small holds for K <= 16384.
+__device__ __forceinline__ float i2f_exact(int acc, bool small) {
+  return small ? __fsub_rn(__int_as_float(acc + 0x4B400000), 12582912.0f) : (float)acc;
+}
+
 // bf16(acc * (w_scale / s_m)), returned widened to fp32.
 __device__ __forceinline__ float scaled_bf16(int acc, float w_scale, float s_m) {
   const float f = __fdiv_rn(w_scale, s_m);
@@ -41,6 +48,20 @@ __device__ __forceinline__ uint16_t relu2_mul_bf16(float g, float u) {
 
 __device__ __forceinline__ uint16_t residual_add_bf16(uint16_t res, float v) {
   return f32_to_bf16_bits(__fadd_rn(bf16_bits_to_f32(res), v));
+}
+
+// The same two steps on packed pairs of bf16 values (element 0 in the low
+// half): the products and sums as .f32x2, each rounding one paired
+// conversion.  Results equal relu2_mul_bf16 / residual_add_bf16 per element.
+__device__ __forceinline__ uint32_t relu2_mul_bf2(uint32_t g, uint32_t u) {
+  const uint64_t gf = f2_from_bf2(g);
+  const uint32_t keep = (__uint_as_float(g << 16) > 0.f ? 0x0000FFFFu : 0u) |
+                        (__uint_as_float(g & 0xFFFF0000u) > 0.f ? 0xFFFF0000u : 0u);
+  const uint32_t r = f2_to_bf2(f2_mul(gf, gf)) & keep;  // relu(g)^2 rounded; +0 where g <= 0
+  return f2_to_bf2(f2_mul(f2_from_bf2(r), f2_from_bf2(u)));
+}
+__device__ __forceinline__ uint32_t residual_add_bf2(uint32_t res, uint32_t v) {
+  return f2_to_bf2(f2_add(f2_from_bf2(res), f2_from_bf2(v)));
 }
 
 }  // namespace bitnet

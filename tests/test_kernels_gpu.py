@@ -233,6 +233,9 @@ def test_bitlinear_tcgen05_decode_shapes(cuda, m, n, k, epilogue, split):
     (1000, 3840, 2560, "none"),           # prefill token tiles of 256, ragged last tile
     (4096, 2560, 6912, "residual_add"),   # down shape over 16 token tiles
     (2048, 1024, 2560, "relu2_mul"),
+    # K > 16384: float(acc) through the conversion instruction instead of the exact 1.5 * 2^23 trick
+    (300, 256, 16448, "relu2_mul"),
+    (300, 384, 16448, "residual_add"),
 ])
 def test_bitlinear_tcgen05_prefill_shapes(cuda, m, n, k, epilogue):
     check_bitlinear(cuda, m, n, k, path=2, epilogue=epilogue, seed=m + n)
