@@ -16,17 +16,15 @@
 //        out[i+64] = bf16(bf16(x[i+64] * cos_i) + bf16( x[i]    * sin_i))
 //      on the G query heads and the new key; the unit whose range holds the
 //      new position writes the rotated key and the value to row positions[b].
-//   2. Warp w takes the 16-key tiles w, w + 4, ... of the range: K and V rows
-//      (4 KB each, contiguous in the cache) arrive by bulk copy into a double
-//      buffer of the warp's own, the first two issued before the RoPE so that
-//      their latency overlaps it; an online softmax runs across the tiles.  Scores q . k_t * scale in fp32
-//      (lane = key x half of the head dimension, 16-byte chunks visited in a
-//      key-rotated order so a shared-memory phase touches 8 bank groups; the
-//      queries are kept as fp32 in a padded layout for the same reason), the
-//      tile's softmax state (max, sum), and P.V (lane = 4 dimensions, the
-//      probabilities broadcast from shared memory).  The tile holding the new
-//      position takes the rotated key and the value from shared memory, not
-//      from the cache row being written.
+//   2. Warp w takes the 16-key tiles w, w + 4, ... of the range: the tile's K
+//      and V rows (4 KB each, contiguous in the cache) arrive by per-lane
+//      16-byte cp.async into an XOR-swizzled double buffer of the warp's own,
+//      the first two issued before the RoPE so that their latency overlaps it.
+//      Per tile, S^T = Q K^T and O^T += V^T P^T run on mma.sync m16n8k16 (K and
+//      V through ldmatrix; P from the score fragments as a bf16 hi + lo pair),
+//      with an online softmax in base 2 across the tiles (see attn_unit).  The
+//      tile holding the new position takes the rotated key and the value from
+//      shared memory, not from the cache row being written.
 //   3. The warps' states merge in shared memory.  With one active unit per
 //      (b, g) the result is normalised and written; otherwise each unit writes
 //      (max, sum, unnormalised accumulator) to the workspace and the last unit
