@@ -11,7 +11,9 @@ kernels use them on):
 * with s = fp32(127 / amax) and |a| <= amax, |fp32(a * s)| < 127.5, so the codes
   need no clamp (`aq_codes4`);
 * rounding a bf16-exact fp32 value to bf16 again changes nothing (the epilogue
-  converts once where it used to round and then convert)."""
+  converts once where it used to round and then convert);
+* in the tiled code layout a row's 8-code chunks are contiguous and 32 chunks
+  apart by a constant 256 T bytes (the prefill act-quant's pointer step)."""
 
 import numpy as np
 
@@ -64,3 +66,26 @@ def test_bf16_rounding_is_idempotent():
     x = (rng.standard_normal(1_000_000) * np.exp(rng.uniform(-20, 20, 1_000_000))).astype(np.float32)
     once = _bf16_round(x)
     np.testing.assert_array_equal(_bf16_round(once), once)
+
+
+def test_code_layout_steps_by_256_tiles_per_32_chunks():
+    """The prefill act-quant stores a row's 8-code chunk ch = lane + 32 i at a
+    pointer that starts at the chunk `lane` and grows by 256 T bytes per step
+    (act_quant_rows_kernel), as one 8-byte store.  Both hold in the device code
+    layout that oracle.bitlinear.act_unlayout reads (token tiles of T rows,
+    inside a tile [K/16][T/8][8 rows][16 bytes])."""
+    from oracle import bitlinear as ob
+
+    for m_rows, k in ((300, 2560), (512, 6912), (256, 128), (264, 14336)):
+        rows, t, kp = ob.act_rows(m_rows), ob.act_tile(m_rows), -(-k // 64) * 64
+        assert t == 256
+        # byte offset of (row, k) in the buffer, by the same reshape as act_unlayout
+        off = np.arange(rows * kp, dtype=np.int64).reshape(rows // t, kp // 16, t // 8, 8, 16)
+        off = off.transpose(0, 2, 3, 1, 4).reshape(rows, kp)
+        chunks = kp // 8
+        for lane in range(min(32, chunks)):
+            ch = np.arange(lane, chunks, 32)
+            start = off[:, 8 * ch]                                        # [rows, steps]
+            np.testing.assert_array_equal(start, off[:, [8 * lane]] + (ch - lane)[None, :] // 32 * 256 * t)
+            for e in range(8):                                            # 8 codes, 8 contiguous bytes
+                np.testing.assert_array_equal(off[:, 8 * ch + e], start + e)
